@@ -1,0 +1,328 @@
+// Seeded noise, perturbation and momentum rebuild for MuZO-Clip on sm_100a.
+//
+// The noise of a parameter block is the stream torch's CUDA generator produces for
+// make_zo_noise_like (muzo_clip/prng.py:39-81): a fresh Philox4x32-10 generator keyed by
+// hash64(step seed, name, shape, block), drawn by a grid-stride launch in which thread t of S
+// fills elements t + S*(4c + j) from the j-th word of its c-th Philox block. The kernels here
+// regenerate exactly those words with cuRAND's Philox device API (curand_init/curand4/
+// curand_normal4 called, not re-implemented) but organise the work for HBM: one work item is 8
+// consecutive threads t..t+7 of one loop trip c, i.e. four 16-byte vectors (j = 0..3) of 8
+// consecutive elements. Warps therefore read and write contiguous 512-byte runs, and the noise
+// never touches memory.
+#include <curand_kernel.h>
+
+#include "muzo_common.cuh"
+
+namespace muzo {
+namespace {
+
+// Noise of 8 consecutive launch threads t0..t0+7 for loop trip `trip`: z[j][k] is element
+// t0 + k + S*(4*trip + j). `word_offset` is the launch's Philox offset (32-bit words).
+template <int DIST>
+__device__ __forceinline__ void noise8x4(uint64_t key, uint64_t t0, uint64_t word_offset,
+                                         uint64_t trip, float (&z)[4][8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    curandStatePhilox4_32_10_t st;
+    curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
+    if (DIST == MUZO_NORMAL) {
+      float4 n = curand_normal4(&st);
+      // randn's transform is rand * std + mean with std = 1, mean = 0
+      z[0][k] = n.x; z[1][k] = n.y; z[2][k] = n.z; z[3][k] = n.w;
+    } else {
+      uint4 r = curand4(&st);
+      // randint(0, 2) keeps word % 2; the reference maps it to 2*b - 1
+      z[0][k] = (r.x & 1u) ? 1.0f : -1.0f;
+      z[1][k] = (r.y & 1u) ? 1.0f : -1.0f;
+      z[2][k] = (r.z & 1u) ? 1.0f : -1.0f;
+      z[3][k] = (r.w & 1u) ? 1.0f : -1.0f;
+    }
+  }
+}
+
+__device__ __forceinline__ int elem_size(int dtype) { return dtype == MUZO_F32 ? 4 : 2; }
+
+__device__ __forceinline__ bool vec_ok(const void* base, int64_t elem_start, int dtype) {
+  uintptr_t a = reinterpret_cast<uintptr_t>(base) + static_cast<uintptr_t>(elem_start) * elem_size(dtype);
+  return (a & 15u) == 0;
+}
+
+struct SegView {
+  char* param;
+  char* out;
+  int64_t numel;
+  int64_t local_item0;  // first item of this CTA relative to the segment
+  uint64_t philox_offset;
+  uint32_t threads;
+  int block;
+};
+
+// Every CTA handles MUZO_ITEMS_PER_CTA consecutive items of exactly one segment.
+__device__ __forceinline__ SegView cta_segment(const muzo_segment* segs, int nsegs, int pdtype, int odtype) {
+  const int64_t item0 = static_cast<int64_t>(blockIdx.x) * MUZO_ITEMS_PER_CTA;
+  const int s = find_segment(segs, nsegs, item0);
+  const muzo_segment& g = segs[s];
+  SegView v;
+  v.param = g.param ? static_cast<char*>(g.param) + g.elem_start * elem_size(pdtype) : nullptr;
+  v.out = g.out ? static_cast<char*>(g.out) + g.elem_start * elem_size(odtype) : nullptr;
+  v.numel = g.numel;
+  v.local_item0 = item0 - g.item_begin;
+  v.philox_offset = g.philox_offset;
+  v.threads = g.threads;
+  v.block = g.block_index;
+  return v;
+}
+
+constexpr int kItemsPerThread = MUZO_ITEMS_PER_CTA / kElemThreads;
+
+// --------------------------------------------------------------------------- fill noise
+
+template <int DIST>
+__global__ void __launch_bounds__(kElemThreads)
+fill_noise_kernel(const muzo_segment* __restrict__ segs, int nsegs, uint64_t key, int odtype) {
+  const SegView sv = cta_segment(segs, nsegs, MUZO_F32, odtype);
+  const uint32_t octets = sv.threads / 8;
+  const bool vec = vec_ok(sv.out, 0, odtype);
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const uint32_t local = static_cast<uint32_t>(sv.local_item0) + it * kElemThreads + threadIdx.x;
+    const uint32_t trip = local / octets;
+    const uint32_t oct = local - trip * octets;
+    const int64_t li0 = static_cast<int64_t>(sv.threads) * (4ll * trip) + 8ll * oct;
+    if (li0 >= sv.numel) continue;
+    float z[4][8];
+    noise8x4<DIST>(key, 8ull * oct, sv.philox_offset, trip, z);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
+      if (li >= sv.numel) break;
+      if (vec && li + 8 <= sv.numel) {
+        store8(sv.out, li, odtype, z[j]);
+      } else {
+        for (int k = 0; k < 8 && li + k < sv.numel; ++k) store_elem(sv.out, li + k, odtype, z[j][k]);
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- perturb
+
+// W <- dtype(W + alpha * dtype(Z)). torch's add_(noise, alpha) evaluates a + alpha * b in fp32,
+// which nvcc contracts to one fused multiply-add.
+template <int DIST, int DTYPE>
+__global__ void __launch_bounds__(kElemThreads)
+perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
+               float alpha) {
+  const SegView sv = cta_segment(segs, nsegs, DTYPE, DTYPE);
+  const uint32_t octets = sv.threads / 8;
+  const bool vec = vec_ok(sv.param, 0, DTYPE);
+  const uint64_t key = keys[sv.block];
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const uint32_t local = static_cast<uint32_t>(sv.local_item0) + it * kElemThreads + threadIdx.x;
+    const uint32_t trip = local / octets;
+    const uint32_t oct = local - trip * octets;
+    const int64_t li0 = static_cast<int64_t>(sv.threads) * (4ll * trip) + 8ll * oct;
+    if (li0 >= sv.numel) continue;
+    float z[4][8];
+    noise8x4<DIST>(key, 8ull * oct, sv.philox_offset, trip, z);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
+      if (li >= sv.numel) break;
+      if (vec && li + 8 <= sv.numel) {
+        float w[8];
+        load8(sv.param, li, DTYPE, w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w[k]);
+        store8(sv.param, li, DTYPE, w);
+      } else {
+        for (int k = 0; k < 8 && li + k < sv.numel; ++k) {
+          float w = load_elem(sv.param, li + k, DTYPE);
+          store_elem(sv.param, li + k, DTYPE, __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w));
+        }
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- rebuild
+
+// Block-wide fp64 reduction of three partial sums followed by one atomicAdd per sum.
+__device__ __forceinline__ void block_accumulate3(double a, double b, double c, double* dst_a,
+                                                  double* dst_b, double* dst_c) {
+  __shared__ double red[3][kElemThreads / 32];
+  a = warp_sum(a); b = warp_sum(b); c = warp_sum(c);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { red[0][warp] = a; red[1][warp] = b; red[2][warp] = c; }
+  __syncthreads();
+  if (warp == 0) {
+    a = lane < kElemThreads / 32 ? red[0][lane] : 0.0;
+    b = lane < kElemThreads / 32 ? red[1][lane] : 0.0;
+    c = lane < kElemThreads / 32 ? red[2][lane] : 0.0;
+    a = warp_sum(a); b = warp_sum(b); c = warp_sum(c);
+    if (lane == 0) {
+      if (a != 0.0) atomicAdd(dst_a, a);
+      if (b != 0.0) atomicAdd(dst_b, b);
+      if (c != 0.0) atomicAdd(dst_c, c);
+    }
+  }
+}
+
+// M = sum_h alphas[h] * float(dtype(Z_h)) (h = age, newest first, as the reference walks
+// reversed(history)); M *= inv_coeff_sum; out = bf16(M). Also sums M^2, bf16(M)^2 and W^2.
+template <int DIST, int PDTYPE>
+__global__ void __launch_bounds__(kElemThreads)
+rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
+               const float* __restrict__ alphas, int horizon, int normalize, float inv_coeff_sum,
+               double* __restrict__ sums, int32_t* __restrict__ flags) {
+  const SegView sv = cta_segment(segs, nsegs, PDTYPE, MUZO_BF16);
+  const uint32_t octets = sv.threads / 8;
+  const bool vec = vec_ok(sv.out, 0, MUZO_BF16) && vec_ok(sv.param, 0, PDTYPE);
+  const uint64_t* bkeys = keys + static_cast<int64_t>(sv.block) * horizon;
+  double m2 = 0.0, x2 = 0.0, w2 = 0.0;
+  bool finite = true;
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const uint32_t local = static_cast<uint32_t>(sv.local_item0) + it * kElemThreads + threadIdx.x;
+    const uint32_t trip = local / octets;
+    const uint32_t oct = local - trip * octets;
+    const int64_t li0 = static_cast<int64_t>(sv.threads) * (4ll * trip) + 8ll * oct;
+    if (li0 >= sv.numel) continue;
+    float acc[4][8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[j][k] = 0.0f;
+#pragma unroll 1
+    for (int h = 0; h < horizon; ++h) {
+      float z[4][8];
+      noise8x4<DIST>(bkeys[h], 8ull * oct, sv.philox_offset, trip, z);
+      const float a = alphas[h];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[j][k] = __fmaf_rn(a, round_to(z[j][k], PDTYPE), acc[j][k]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
+      if (li >= sv.numel) break;
+      float m[8], w[8];
+      const int cnt = li + 8 <= sv.numel ? 8 : static_cast<int>(sv.numel - li);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m[k] = normalize ? acc[j][k] * inv_coeff_sum : acc[j][k];
+      if (vec && cnt == 8) {
+        load8(sv.param, li, PDTYPE, w);
+        store8(sv.out, li, MUZO_BF16, m);
+      } else {
+        for (int k = 0; k < 8; ++k) w[k] = k < cnt ? load_elem(sv.param, li + k, PDTYPE) : 0.0f;
+        for (int k = 0; k < cnt; ++k) store_elem(sv.out, li + k, MUZO_BF16, m[k]);
+      }
+      float pm = 0.0f, px = 0.0f, pw = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k < cnt) {
+          finite = finite && isfinite(m[k]);
+          const float xb = bf16r(m[k]);
+          pm = __fmaf_rn(m[k], m[k], pm);
+          px = __fmaf_rn(xb, xb, px);
+          pw = __fmaf_rn(w[k], w[k], pw);
+        }
+      }
+      m2 += pm; x2 += px; w2 += pw;
+    }
+  }
+  double* bs = sums + static_cast<int64_t>(sv.block) * MUZO_NSUMS;
+  block_accumulate3(m2, x2, w2, bs + MUZO_SUM_M2, bs + MUZO_SUM_X2, bs + MUZO_SUM_W2);
+  if (!finite) atomicOr(flags + sv.block, MUZO_FLAG_NONFINITE_INPUT);
+}
+
+bool valid_dtype(int d) { return d == MUZO_F32 || d == MUZO_BF16 || d == MUZO_F16; }
+
+template <typename F>
+int dispatch_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case MUZO_F32: f(std::integral_constant<int, MUZO_F32>()); return MUZO_OK;
+    case MUZO_BF16: f(std::integral_constant<int, MUZO_BF16>()); return MUZO_OK;
+    case MUZO_F16: f(std::integral_constant<int, MUZO_F16>()); return MUZO_OK;
+    default: return MUZO_ERR_DTYPE;
+  }
+}
+
+int check_table(const muzo_segment* segs, int nsegs, int64_t total_items) {
+  if (segs == nullptr || nsegs <= 0 || total_items <= 0 || total_items % MUZO_ITEMS_PER_CTA != 0)
+    return MUZO_ERR_ARG;
+  if (total_items / MUZO_ITEMS_PER_CTA > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;
+  return MUZO_OK;
+}
+
+}  // namespace
+}  // namespace muzo
+
+using namespace muzo;
+
+extern "C" {
+
+int muzo_fill_noise(const muzo_segment* d_segs, int nsegs, int64_t total_items, uint64_t key,
+                    int dist, int out_dtype, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_table(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (!valid_dtype(out_dtype)) return MUZO_ERR_DTYPE;
+  const dim3 grid(static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dist == MUZO_NORMAL)
+    fill_noise_kernel<MUZO_NORMAL><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, key, out_dtype);
+  else if (dist == MUZO_RADEMACHER)
+    fill_noise_kernel<MUZO_RADEMACHER><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, key, out_dtype);
+  else
+    return MUZO_ERR_ARG;
+  return launch_status();
+}
+
+int muzo_perturb_segments(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                          const uint64_t* d_keys, int dtype, int dist, float alpha, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_table(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_keys == nullptr || (dist != MUZO_NORMAL && dist != MUZO_RADEMACHER)) return MUZO_ERR_ARG;
+  const dim3 grid(static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dispatch_dtype(dtype, [&](auto d) {
+    constexpr int D = decltype(d)::value;
+    if (dist == MUZO_NORMAL)
+      perturb_kernel<MUZO_NORMAL, D><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_keys, alpha);
+    else
+      perturb_kernel<MUZO_RADEMACHER, D><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_keys, alpha);
+  });
+  if (st != MUZO_OK) return st;
+  return launch_status();
+}
+
+int muzo_rebuild_segments(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                          const uint64_t* d_keys, const float* d_alphas, int horizon, int dist,
+                          int param_dtype, int normalize, float inv_coeff_sum, double* d_sums,
+                          int32_t* d_flags, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_table(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_keys == nullptr || d_alphas == nullptr || d_sums == nullptr || d_flags == nullptr ||
+      horizon <= 0 || (dist != MUZO_NORMAL && dist != MUZO_RADEMACHER))
+    return MUZO_ERR_ARG;
+  const dim3 grid(static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dispatch_dtype(param_dtype, [&](auto d) {
+    constexpr int D = decltype(d)::value;
+    if (dist == MUZO_NORMAL)
+      rebuild_kernel<MUZO_NORMAL, D><<<grid, kElemThreads, 0, s>>>(
+          d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags);
+    else
+      rebuild_kernel<MUZO_RADEMACHER, D><<<grid, kElemThreads, 0, s>>>(
+          d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags);
+  });
+  if (st != MUZO_OK) return st;
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,369 @@
+// Element-wise step kernels around the Newton-Schulz GEMMs: normalisation of the rebuilt
+// momentum, the update's sum of squares, the fused scale / ratio-clip / apply / weight-decay
+// write-back, and the QK-Clip row scaling. All are HBM-bound streams over linear segments
+// (muzo_plan_linear), 8 elements (one 16-byte vector of bf16) per work item.
+#include "muzo_common.cuh"
+
+namespace muzo {
+namespace {
+
+constexpr int kItemsPerThread = MUZO_ITEMS_PER_CTA / kElemThreads;
+
+struct LinView {
+  char* param;
+  char* out;
+  int64_t numel;
+  int64_t local_item0;
+  int block;
+};
+
+__device__ __forceinline__ LinView cta_linear(const muzo_segment* segs, int nsegs) {
+  const int64_t item0 = static_cast<int64_t>(blockIdx.x) * MUZO_ITEMS_PER_CTA;
+  const int s = find_segment(segs, nsegs, item0);
+  const muzo_segment& g = segs[s];
+  LinView v;
+  v.param = static_cast<char*>(g.param);
+  v.out = static_cast<char*>(g.out);
+  v.numel = g.numel;
+  v.local_item0 = item0 - g.item_begin;
+  v.block = g.block_index;
+  return v;
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+__device__ __forceinline__ double block_sum(double v) {
+  __shared__ double red[kElemThreads / 32];
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double r = 0.0;
+  if (warp == 0) {
+    r = lane < kElemThreads / 32 ? red[lane] : 0.0;
+    r = warp_sum(r);
+  }
+  return r;  // valid in thread 0
+}
+
+// ------------------------------------------------------------------ normalisation
+// X <- bf16(X / (||X||_F + 1e-7)) (newton_schulz.py:46-53): the norm is the fp32 Frobenius norm
+// of the bf16 values, 1e-7 is added in fp32 and the division is IEEE round-to-nearest.
+__global__ void __launch_bounds__(kElemThreads)
+ns_normalize_kernel(const muzo_segment* __restrict__ segs, int nsegs, const double* __restrict__ sums,
+                    int32_t* __restrict__ flags) {
+  const LinView v = cta_linear(segs, nsegs);
+  const double* bs = sums + static_cast<int64_t>(v.block) * MUZO_NSUMS;
+  const double m2 = bs[MUZO_SUM_M2];
+  const float nrm = static_cast<float>(sqrt(bs[MUZO_SUM_X2]));
+  const float denom = __fadd_rn(nrm, 1e-7f);
+  // zeropower_via_newtonschulz5 returns zeros for a zero or non-finite fp32 norm (35-43)
+  if (v.local_item0 == 0 && threadIdx.x == 0 && (!(m2 > 0.0) || !isfinite(m2)))
+    atomicOr(flags + v.block, MUZO_FLAG_ZERO_NORM);
+  const bool vec = aligned16(v.out);
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const int64_t item = v.local_item0 + it * kElemThreads + threadIdx.x;
+    const int64_t li = item * 8;
+    if (li >= v.numel) break;
+    if (vec && li + 8 <= v.numel) {
+      float x[8];
+      load8(v.out, li, MUZO_BF16, x);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = __fdiv_rn(x[k], denom);
+      store8(v.out, li, MUZO_BF16, x);
+    } else {
+      for (int k = 0; k < 8 && li + k < v.numel; ++k)
+        store_elem(v.out, li + k, MUZO_BF16, __fdiv_rn(load_elem(v.out, li + k, MUZO_BF16), denom));
+    }
+  }
+}
+
+// ------------------------------------------------------------------ prepare
+// Newton-Schulz input from an arbitrary matrix G (newton_schulz.py:35-46): X = bf16(G) and the
+// sums of fp32(G)^2 and X^2; a non-finite G sets MUZO_FLAG_NONFINITE_INPUT.
+template <int DTYPE>
+__global__ void __launch_bounds__(kElemThreads)
+ns_prepare_kernel(const muzo_segment* __restrict__ segs, int nsegs, double* __restrict__ sums,
+                  int32_t* __restrict__ flags) {
+  const LinView v = cta_linear(segs, nsegs);
+  const bool vec = aligned16(v.out) && aligned16(v.param);
+  double m2 = 0.0, x2 = 0.0;
+  bool finite = true;
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const int64_t item = v.local_item0 + it * kElemThreads + threadIdx.x;
+    const int64_t li = item * 8;
+    if (li >= v.numel) break;
+    const int cnt = li + 8 <= v.numel ? 8 : static_cast<int>(v.numel - li);
+    float g[8];
+    if (vec && cnt == 8) load8(v.param, li, DTYPE, g);
+    else for (int k = 0; k < 8; ++k) g[k] = k < cnt ? load_elem(v.param, li + k, DTYPE) : 0.0f;
+    float pm = 0.0f, px = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      finite = finite && isfinite(g[k]);
+      const float xb = bf16r(g[k]);
+      pm = __fmaf_rn(g[k], g[k], pm);
+      px = __fmaf_rn(xb, xb, px);
+    }
+    m2 += pm; x2 += px;
+    if (vec && cnt == 8) store8(v.out, li, MUZO_BF16, g);
+    else for (int k = 0; k < cnt; ++k) store_elem(v.out, li + k, MUZO_BF16, g[k]);
+  }
+  double* bs = sums + static_cast<int64_t>(v.block) * MUZO_NSUMS;
+  const double tm = block_sum(m2);
+  const double tx = block_sum(x2);
+  if (threadIdx.x == 0) {
+    if (tm != 0.0) atomicAdd(bs + MUZO_SUM_M2, tm);
+    if (tx != 0.0) atomicAdd(bs + MUZO_SUM_X2, tx);
+  }
+  if (!finite) atomicOr(flags + v.block, MUZO_FLAG_NONFINITE_INPUT);
+}
+
+// ------------------------------------------------------------------ sum of U^2
+// U = fp32(X) * scale (muzo_optimizer.py:340); sums U^2 and flags a non-finite X
+// (newton_schulz.py:63-65).
+__global__ void __launch_bounds__(kElemThreads)
+update_sumsq_kernel(const muzo_segment* __restrict__ segs, int nsegs, const float* __restrict__ scales,
+                    double* __restrict__ sums, int32_t* __restrict__ flags) {
+  const LinView v = cta_linear(segs, nsegs);
+  const float scale = scales[v.block];
+  const bool vec = aligned16(v.out);
+  double acc = 0.0;
+  bool finite = true;
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const int64_t item = v.local_item0 + it * kElemThreads + threadIdx.x;
+    const int64_t li = item * 8;
+    if (li >= v.numel) break;
+    float x[8];
+    const int cnt = li + 8 <= v.numel ? 8 : static_cast<int>(v.numel - li);
+    if (vec && cnt == 8) load8(v.out, li, MUZO_BF16, x);
+    else for (int k = 0; k < 8; ++k) x[k] = k < cnt ? load_elem(v.out, li + k, MUZO_BF16) : 0.0f;
+    float p = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      finite = finite && isfinite(x[k]);
+      const float u = x[k] * scale;
+      p = __fmaf_rn(u, u, p);
+    }
+    acc += p;
+  }
+  const double tot = block_sum(acc);
+  if (threadIdx.x == 0 && tot != 0.0)
+    atomicAdd(sums + static_cast<int64_t>(v.block) * MUZO_NSUMS + MUZO_SUM_U2, tot);
+  if (!finite) atomicOr(flags + v.block, MUZO_FLAG_NONFINITE_OUTPUT);
+}
+
+// ------------------------------------------------------------------ apply
+struct ApplyScalars {
+  float clip;     // multiplier applied to U
+  bool clipped;
+  bool zeroed;
+  float ratio;    // ratio before the clip
+};
+
+// Per-block scalars of muzo_optimizer.py:342-349, recomputed by every CTA of the block.
+__device__ __forceinline__ ApplyScalars block_scalars(const double* bs, int32_t flag, int64_t numel,
+                                                      float lr, double ratio_clip) {
+  ApplyScalars s;
+  s.zeroed = (flag & (MUZO_FLAG_NONFINITE_INPUT | MUZO_FLAG_ZERO_NORM | MUZO_FLAG_NONFINITE_OUTPUT)) != 0;
+  const double n = static_cast<double>(numel);
+  const float rms_u = s.zeroed ? 0.0f : static_cast<float>(sqrt(bs[MUZO_SUM_U2] / n));
+  const float rms_w = static_cast<float>(sqrt(bs[MUZO_SUM_W2] / n));
+  const float update_rms = rms_u * lr;
+  const float ratio = __fdiv_rn(update_rms, __fadd_rn(rms_w, 1e-12f));
+  s.ratio = ratio;
+  s.clipped = static_cast<double>(ratio) > ratio_clip;
+  s.clip = s.clipped ? static_cast<float>(ratio_clip / static_cast<double>(ratio)) : 1.0f;
+  return s;
+}
+
+template <int DTYPE>
+__global__ void __launch_bounds__(kElemThreads)
+apply_update_kernel(const muzo_segment* __restrict__ segs, int nsegs, const float* __restrict__ scales,
+                    float lr, double ratio_clip, int apply_decay, float decay,
+                    double* __restrict__ sums, const int32_t* __restrict__ flags,
+                    float* __restrict__ stats) {
+  const LinView v = cta_linear(segs, nsegs);
+  double* bs = sums + static_cast<int64_t>(v.block) * MUZO_NSUMS;
+  const ApplyScalars sc = block_scalars(bs, flags[v.block], v.numel, lr, ratio_clip);
+  const float scale = scales[v.block];
+  const float neg_lr = -lr;
+  if (v.local_item0 == 0 && threadIdx.x == 0) {
+    float* st = stats + static_cast<int64_t>(v.block) * MUZO_NSTATS;
+    st[MUZO_STAT_RATIO_BEFORE] = sc.ratio;
+    st[MUZO_STAT_CLIP_FACTOR] = sc.clip;
+    st[MUZO_STAT_ZEROED] = sc.zeroed ? 1.0f : 0.0f;
+  }
+  const bool vec = aligned16(v.out) && aligned16(v.param);
+  double acc = 0.0;
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const int64_t item = v.local_item0 + it * kElemThreads + threadIdx.x;
+    const int64_t li = item * 8;
+    if (li >= v.numel) break;
+    const int cnt = li + 8 <= v.numel ? 8 : static_cast<int>(v.numel - li);
+    float x[8], w[8];
+    if (vec && cnt == 8) {
+      load8(v.out, li, MUZO_BF16, x);
+      load8(v.param, li, DTYPE, w);
+    } else {
+      for (int k = 0; k < 8; ++k) {
+        x[k] = k < cnt ? load_elem(v.out, li + k, MUZO_BF16) : 0.0f;
+        w[k] = k < cnt ? load_elem(v.param, li + k, DTYPE) : 0.0f;
+      }
+    }
+    float p = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float u = sc.zeroed ? 0.0f : x[k] * scale;       // U.mul_(sqrt(max)*muon_scale)
+      if (sc.clipped) u = u * sc.clip;                  // U.mul_(clip / ratio)
+      if (k < cnt) p = __fmaf_rn(u, u, p);
+      const float ud = round_to(u, DTYPE);              // U.to(block.dtype)
+      float nw = round_to(__fmaf_rn(neg_lr, ud, w[k]), DTYPE);  // block.add_(U, alpha=-lr)
+      if (apply_decay) nw = round_to(nw * decay, DTYPE);        // block.mul_(1 - lr*wd)
+      w[k] = nw;
+    }
+    acc += p;
+    if (vec && cnt == 8) store8(v.param, li, DTYPE, w);
+    else for (int k = 0; k < cnt; ++k) store_elem(v.param, li + k, DTYPE, w[k]);
+  }
+  const double tot = block_sum(acc);
+  if (threadIdx.x == 0 && tot != 0.0) atomicAdd(bs + MUZO_SUM_U2_CLIPPED, tot);
+}
+
+// ------------------------------------------------------------------ QK-Clip row scaling
+template <int DTYPE>
+__global__ void qk_scale_rows_kernel(char* __restrict__ w, int64_t groups, int64_t rows_per_group,
+                                     int64_t cols, const float* __restrict__ factors,
+                                     const int32_t* __restrict__ mask) {
+  const int64_t total = groups * rows_per_group * cols;
+  const int64_t per_group = rows_per_group * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t g = i / per_group;
+    if (mask[g] == 0) continue;
+    store_elem(w, i, DTYPE, load_elem(w, i, DTYPE) * factors[g]);
+  }
+}
+
+int check_linear(const muzo_segment* segs, int nsegs, int64_t total_items) {
+  if (segs == nullptr || nsegs <= 0 || total_items <= 0 || total_items % MUZO_ITEMS_PER_CTA != 0)
+    return MUZO_ERR_ARG;
+  if (total_items / MUZO_ITEMS_PER_CTA > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;
+  return MUZO_OK;
+}
+
+}  // namespace
+}  // namespace muzo
+
+using namespace muzo;
+
+extern "C" {
+
+int muzo_ns_normalize(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                      const double* d_sums, int32_t* d_flags, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_linear(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_sums == nullptr || d_flags == nullptr) return MUZO_ERR_ARG;
+  ns_normalize_kernel<<<static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA), kElemThreads, 0,
+                        static_cast<cudaStream_t>(stream)>>>(d_segs, nsegs, d_sums, d_flags);
+  return launch_status();
+}
+
+int muzo_ns_prepare(const muzo_segment* d_segs, int nsegs, int64_t total_items, int dtype,
+                    double* d_sums, int32_t* d_flags, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_linear(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_sums == nullptr || d_flags == nullptr) return MUZO_ERR_ARG;
+  const unsigned grid = static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case MUZO_BF16: ns_prepare_kernel<MUZO_BF16><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_sums, d_flags); break;
+    case MUZO_F16: ns_prepare_kernel<MUZO_F16><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_sums, d_flags); break;
+    case MUZO_F32: ns_prepare_kernel<MUZO_F32><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_sums, d_flags); break;
+    default: return MUZO_ERR_DTYPE;
+  }
+  return launch_status();
+}
+
+int muzo_update_sumsq(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                      const float* d_scales, double* d_sums, int32_t* d_flags, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_linear(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_scales == nullptr || d_sums == nullptr || d_flags == nullptr) return MUZO_ERR_ARG;
+  update_sumsq_kernel<<<static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA), kElemThreads, 0,
+                        static_cast<cudaStream_t>(stream)>>>(d_segs, nsegs, d_scales, d_sums, d_flags);
+  return launch_status();
+}
+
+int muzo_apply_update(const muzo_segment* d_segs, int nsegs, int64_t total_items, int dtype,
+                      const float* d_scales, float lr, double ratio_clip, int apply_decay,
+                      float decay, double* d_sums, const int32_t* d_flags, float* d_stats,
+                      void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_linear(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_scales == nullptr || d_sums == nullptr || d_flags == nullptr || d_stats == nullptr)
+    return MUZO_ERR_ARG;
+  const unsigned grid = static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case MUZO_BF16:
+      apply_update_kernel<MUZO_BF16><<<grid, kElemThreads, 0, s>>>(
+          d_segs, nsegs, d_scales, lr, ratio_clip, apply_decay, decay, d_sums, d_flags, d_stats);
+      break;
+    case MUZO_F16:
+      apply_update_kernel<MUZO_F16><<<grid, kElemThreads, 0, s>>>(
+          d_segs, nsegs, d_scales, lr, ratio_clip, apply_decay, decay, d_sums, d_flags, d_stats);
+      break;
+    case MUZO_F32:
+      apply_update_kernel<MUZO_F32><<<grid, kElemThreads, 0, s>>>(
+          d_segs, nsegs, d_scales, lr, ratio_clip, apply_decay, decay, d_sums, d_flags, d_stats);
+      break;
+    default:
+      return MUZO_ERR_DTYPE;
+  }
+  return launch_status();
+}
+
+int muzo_qk_scale_rows(void* w, int dtype, int64_t groups, int64_t rows_per_group, int64_t cols,
+                       const float* d_factors, const int32_t* d_mask, void* stream) {
+  if (w == nullptr || d_factors == nullptr || d_mask == nullptr || groups < 0 ||
+      rows_per_group < 0 || cols < 0)
+    return MUZO_ERR_ARG;
+  const int64_t total = groups * rows_per_group * cols;
+  if (total == 0) return MUZO_OK;
+  int64_t blocks = (total + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* p = static_cast<char*>(w);
+  switch (dtype) {
+    case MUZO_BF16:
+      qk_scale_rows_kernel<MUZO_BF16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+          p, groups, rows_per_group, cols, d_factors, d_mask);
+      break;
+    case MUZO_F16:
+      qk_scale_rows_kernel<MUZO_F16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+          p, groups, rows_per_group, cols, d_factors, d_mask);
+      break;
+    case MUZO_F32:
+      qk_scale_rows_kernel<MUZO_F32><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+          p, groups, rows_per_group, cols, d_factors, d_mask);
+      break;
+    default:
+      return MUZO_ERR_DTYPE;
+  }
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,417 @@
+"""Device-side engine of MuZOClipOptimizer: launch tables, key uploads and the step pipeline.
+
+Everything model-sized stays on the GPU. Per perturbation pass the host computes one 63-bit key
+per parameter block (cached per seed), uploads them, and one kernel launch per parameter dtype
+regenerates the noise and updates every block in place. Per step the owned blocks are processed
+in batches of equal shape: rebuild -> normalise -> Newton-Schulz GEMMs -> sum of squares ->
+apply, and the step statistics come back in one device-to-host copy.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from .newton_schulz import NSBuffers, allocate_ns_buffers, ns_iterations
+from .prng import hash64_seed, iter_param_blocks
+
+DEFAULT_WORKSPACE_BYTES = 16 << 30
+
+
+@dataclass
+class Block:
+    index: int              # position in the optimizer's block list
+    name: str
+    block_index: int
+    tensor: torch.Tensor    # view into param.data
+    rows: int
+    cols: int
+    dtype: torch.dtype
+
+    @property
+    def numel(self) -> int:
+        return self.rows * self.cols
+
+    def key(self, seed: int) -> int:
+        return hash64_seed(seed, self.name, (self.rows, self.cols), self.block_index)
+
+
+@dataclass
+class PerturbGroup:
+    dtype_code: int
+    blocks: list[Block]
+    table: torch.Tensor
+    nsegs: int
+    total_items: int
+
+
+@dataclass
+class Chunk:
+    blocks: list[Block]
+    rows: int
+    cols: int
+    dtype_code: int
+    slot0: int                   # first index of this chunk in the step's per-block arrays
+    rebuild_table: torch.Tensor
+    rebuild_nsegs: int
+    rebuild_items: int
+    norm_table: torch.Tensor
+    norm_items: int
+    apply_tables: dict[int, tuple[torch.Tensor, int]] = field(default_factory=dict)  # by parity
+    scales: torch.Tensor | None = None
+    pad_views: list[torch.Tensor] | None = None
+
+
+class _Uploader:
+    """Ring of pinned host staging buffers for small per-step uploads (keys, coefficients)."""
+
+    def __init__(self, device: torch.device, nbytes: int, depth: int = 4):
+        self.device = device
+        self.nbytes = max(int(nbytes), 64)
+        self.host = [torch.empty(self.nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(depth)]
+        self.dev = [torch.empty(self.nbytes, dtype=torch.uint8, device=device) for _ in range(depth)]
+        self.events = [None] * depth
+        self.i = 0
+
+    def upload(self, arr: np.ndarray) -> torch.Tensor:
+        raw = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
+        if raw.size > self.nbytes:
+            raise ValueError("upload larger than the staging buffer")
+        i = self.i
+        self.i = (i + 1) % len(self.host)
+        if self.events[i] is not None:
+            self.events[i].synchronize()
+        h = self.host[i]
+        h[: raw.size].numpy()[:] = raw
+        d = self.dev[i]
+        d[: raw.size].copy_(h[: raw.size], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.events[i] = ev
+        return d
+
+
+def ns_flops(rows: int, cols: int, steps: int) -> float:
+    """Dense FLOPs of the quintic iteration on one rows x cols matrix: 5 * (4 m^2 n + 2 m^3)."""
+    m, n = min(rows, cols), max(rows, cols)
+    return float(steps) * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def partition_blocks(costs: Sequence[float], world: int) -> list[int]:
+    """Owner rank of every block: longest-processing-time greedy over the given costs
+    (ties resolved by block index, so every rank computes the same assignment)."""
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    load = [0.0] * world
+    owner = [0] * len(costs)
+    for i in order:
+        r = min(range(world), key=lambda q: (load[q], q))
+        owner[i] = r
+        load[r] += costs[i]
+    return owner
+
+
+class StepEngine:
+    def __init__(self, opt, rank: int = 0, world: int = 1, process_group=None):
+        self.opt = opt
+        self.rank = rank
+        self.world = world
+        self.pg = process_group
+        blocks: list[Block] = []
+        for sel in opt.selected_params:
+            data = sel.param.data
+            if data.device.type != "cuda":
+                raise ValueError(f"muzo_clip_b200 needs CUDA parameters; {sel.name} is on {data.device}")
+            for bi, _, view in iter_param_blocks(data, opt.block_rows):
+                if not view.is_contiguous():
+                    raise ValueError(f"parameter block {sel.name}[{bi}] is not contiguous")
+                _lib.dtype_code(view.dtype)
+                blocks.append(Block(len(blocks), sel.name, bi, view, int(view.shape[0]), int(view.shape[1]),
+                                    view.dtype))
+        self.blocks = blocks
+        self.device = blocks[0].tensor.device if blocks else torch.device("cuda")
+        self.fingerprint = self._fingerprint(opt)
+        self.dist = _lib.dist_code(opt.distribution)
+        self.sms, self.max_thr = _lib.device_geometry(self.device)
+        self._key_cache: dict[int, np.ndarray] = {}
+        self._build_perturb_groups()
+        costs = [ns_flops(b.rows, b.cols, max(opt.ns_steps, 1)) for b in blocks]
+        self.owner = partition_blocks(costs, world) if world > 1 else [0] * len(blocks)
+        self.owned = [b for b in blocks if self.owner[b.index] == rank]
+        self._step_ready = False
+        self._phase_events = None
+        horizon = max(opt.horizon, 1)
+        self.uploader = _Uploader(self.device, 8 * (len(blocks) * (horizon + 1) + 64))
+
+    # ------------------------------------------------------------------ bookkeeping
+    @staticmethod
+    def _fingerprint(opt) -> tuple:
+        return tuple((s.name, s.param.data.data_ptr(), tuple(s.param.shape), s.param.dtype)
+                     for s in opt.selected_params) + (opt.block_rows, opt.distribution)
+
+    def matches(self, opt) -> bool:
+        return self.fingerprint == self._fingerprint(opt)
+
+    def keys_for(self, seed: int) -> np.ndarray:
+        keys = self._key_cache.get(seed)
+        if keys is None:
+            keys = np.fromiter((b.key(seed) for b in self.blocks), dtype=np.uint64, count=len(self.blocks))
+            if len(self._key_cache) > self.opt.horizon + 4:
+                self._key_cache.pop(next(iter(self._key_cache)))
+            self._key_cache[seed] = keys
+        return keys
+
+    # ------------------------------------------------------------------ perturbation
+    def _build_perturb_groups(self) -> None:
+        groups: dict[int, list[Block]] = {}
+        for b in self.blocks:
+            groups.setdefault(_lib.dtype_code(b.dtype), []).append(b)
+        self.perturb_groups: list[PerturbGroup] = []
+        for code, blks in groups.items():
+            segs, total = _lib.plan_segments([b.numel for b in blks], [b.tensor.data_ptr() for b in blks],
+                                             None, self.dist, self.sms, self.max_thr)
+            # block_index in the table indexes the group's key array
+            table = _lib.to_device_table(segs, self.device)
+            self.perturb_groups.append(PerturbGroup(code, blks, table, len(segs), total))
+
+    def perturb(self, seed: int, alpha: float) -> None:
+        """W <- W + alpha * Z(seed) for every selected block (muzo_optimizer.py:434-446)."""
+        if not self.blocks:
+            return
+        keys = self.keys_for(seed)
+        stream = _lib.stream_ptr(self.device)
+        dev_keys = self.uploader.upload(keys)
+        alpha32 = float(np.float32(alpha))
+        for g in self.perturb_groups:
+            idx = np.fromiter((b.index for b in g.blocks), dtype=np.int64, count=len(g.blocks))
+            if len(self.perturb_groups) == 1 and np.array_equal(idx, np.arange(len(self.blocks))):
+                kptr = dev_keys.data_ptr()
+            else:
+                kptr = self.uploader.upload(keys[idx]).data_ptr()
+            _lib.launch("muzo_perturb_segments", g.table.data_ptr(), g.nsegs, g.total_items, kptr,
+                                               g.dtype_code, self.dist, alpha32, stream)
+
+    # ------------------------------------------------------------------ step
+    def _workspace_budget(self) -> int:
+        budget = getattr(self.opt, "workspace_bytes", None) or DEFAULT_WORKSPACE_BYTES
+        try:
+            free, _ = torch.cuda.mem_get_info(self.device)
+            budget = min(budget, int(free * 0.5))
+        except RuntimeError:
+            pass
+        return max(budget, 1)
+
+    def _build_step(self) -> None:
+        opt = self.opt
+        # classes in first-appearance order over ALL blocks, so every rank walks them alike
+        self.class_order: list[tuple[int, int, int]] = []
+        for b in self.blocks:
+            ck = (b.rows, b.cols, _lib.dtype_code(b.dtype))
+            if ck not in self.class_order:
+                self.class_order.append(ck)
+        classes: dict[tuple[int, int, int], list[Block]] = {ck: [] for ck in self.class_order}
+        for b in self.owned:
+            classes[(b.rows, b.cols, _lib.dtype_code(b.dtype))].append(b)
+        classes = {ck: v for ck, v in classes.items() if v}
+        budget = self._workspace_budget()
+        per_block_max = 0
+        plans = []
+        for (rows, cols, code), blks in classes.items():
+            m = min(rows, cols)
+            per_block = 2 * rows * ((cols + 7) // 8 * 8) * 2 + 2 * m * ((m + 7) // 8 * 8) * 2
+            chunk = max(1, min(len(blks), budget // max(per_block, 1)))
+            plans.append((rows, cols, code, blks, chunk))
+            per_block_max = max(per_block_max, per_block * chunk)
+        self.chunks: list[Chunk] = []
+        self.buffers: dict[tuple[int, int], NSBuffers] = {}
+        slot = 0
+        for rows, cols, code, blks, chunk in plans:
+            buf = allocate_ns_buffers(rows, cols, chunk, self.device)
+            self.buffers[(rows, cols, code)] = buf
+            for start in range(0, len(blks), chunk):
+                part = blks[start:start + chunk]
+                n = len(part)
+                dense = buf.ld == cols
+                # rebuild and normalise write X0 densely; padded layouts go through a staging copy
+                if dense:
+                    x0_ptrs = [buf.x_slot(0)[i].data_ptr() for i in range(n)]
+                    pad_views = None
+                else:
+                    stage = torch.empty((n, rows, cols), dtype=torch.bfloat16, device=self.device)
+                    x0_ptrs = [stage[i].data_ptr() for i in range(n)]
+                    pad_views = [stage]
+                rsegs, rtot = _lib.plan_segments([b.numel for b in part], [b.tensor.data_ptr() for b in part],
+                                                 x0_ptrs, self.dist, self.sms, self.max_thr)
+                nsegs, ntot = _lib.plan_linear([b.numel for b in part], x0_ptrs, x0_ptrs)
+                ch = Chunk(part, rows, cols, code, slot, _lib.to_device_table(rsegs, self.device), len(rsegs),
+                           rtot, _lib.to_device_table(nsegs, self.device), ntot, pad_views=pad_views)
+                for parity in (0, 1):
+                    xs = buf.x_slot(parity)
+                    outs = [xs[i].data_ptr() for i in range(n)] if dense else [stage[i].data_ptr() for i in range(n)]
+                    asegs, atot = _lib.plan_linear([b.numel for b in part], [b.tensor.data_ptr() for b in part], outs)
+                    ch.apply_tables[parity] = (_lib.to_device_table(asegs, self.device), atot)
+                scales = np.asarray([math.sqrt(max(b.rows, b.cols)) * opt.muon_scale for b in part], dtype=np.float32)
+                ch.scales = torch.from_numpy(scales).to(self.device)
+                self.chunks.append(ch)
+                slot += n
+        self.n_slots = slot
+        # one zeroed device buffer per step: sums (f64), flags + status (i32), stats (f32)
+        self.sums_bytes = 8 * _lib.NSUMS * max(slot, 1)
+        self.flags_off = self.sums_bytes
+        self.stats_off = self.flags_off + 4 * (max(slot, 1) + 4)
+        self.stats_off = (self.stats_off + 15) // 16 * 16
+        self.state_bytes = self.stats_off + 4 * _lib.NSTATS * max(slot, 1)
+        self.state = torch.zeros(self.state_bytes, dtype=torch.uint8, device=self.device)
+        self._step_ready = True
+
+    def owned_ns_flops(self) -> float:
+        return sum(ns_flops(b.rows, b.cols, self.opt.ns_steps) for b in self.owned)
+
+    def profile_step(self, history, lr: float) -> dict[str, float]:
+        """Run one step with CUDA events around each phase; returns milliseconds per phase
+        (summed over chunks). Applies the update like run_step."""
+        self._phase_events: dict[str, list] = {}
+        try:
+            self.run_step(history, lr)
+            torch.cuda.synchronize(self.device)
+            return {k: sum(a.elapsed_time(b) for a, b in v) for k, v in self._phase_events.items()}
+        finally:
+            self._phase_events = None
+
+    def _mark(self, phase: str, start: bool) -> None:
+        ev_map = getattr(self, "_phase_events", None)
+        if ev_map is None:
+            return
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        if start:
+            ev_map.setdefault(phase, []).append([ev, None])
+        else:
+            ev_map[phase][-1][1] = ev
+
+    def run_step(self, history, lr: float) -> dict[int, dict[str, float]]:
+        """Rebuild, orthogonalise and apply the update of every owned block. Returns per-block
+        statistics keyed by block index (owned blocks only)."""
+        opt = self.opt
+        if not self._step_ready:
+            self._build_step()
+        hist = list(reversed(history))
+        horizon = len(hist)
+        coeffs = [opt.beta_momentum ** age for age in range(horizon)]
+        coeff_sum = 0.0
+        for c in coeffs:
+            coeff_sum += c
+        alphas = np.asarray([c * item.p for c, item in zip(coeffs, hist)], dtype=np.float32)
+        normalize = 1 if (opt.normalize_momentum and coeff_sum > 0) else 0
+        inv_cs = float(np.float32(1.0) / np.float32(coeff_sum)) if normalize else 1.0
+        stream = _lib.stream_ptr(self.device)
+        device = self.device
+
+        # keys of every owned block for every history item, chunk-major: [slot, age]
+        seed_keys = [self.keys_for(item.seed) for item in hist]
+        order = np.fromiter((b.index for ch in self.chunks for b in ch.blocks), dtype=np.int64,
+                            count=self.n_slots)
+        keys = np.stack([k[order] for k in seed_keys], axis=1) if horizon else np.zeros((0, 0), np.uint64)
+        payload = np.concatenate([keys.reshape(-1).view(np.uint8), alphas.view(np.uint8)])
+        dev = self.uploader.upload(payload)
+        keys_ptr = dev.data_ptr()
+        alphas_ptr = keys_ptr + keys.size * 8
+
+        self.state.zero_()
+        base = self.state.data_ptr()
+        sums_ptr, flags_ptr, stats_ptr = base, base + self.flags_off, base + self.stats_off
+        status_ptr = flags_ptr + 4 * (max(self.n_slots, 1))
+        lr32 = float(np.float32(lr))
+        decay = float(np.float32(1.0 - lr * opt.weight_decay))
+        apply_decay = 1 if opt.weight_decay else 0
+        chunks_by_class: dict[tuple[int, int, int], list[Chunk]] = {}
+        for ch in self.chunks:
+            chunks_by_class.setdefault((ch.rows, ch.cols, ch.dtype_code), []).append(ch)
+        for ck in self.class_order:
+            for ch in chunks_by_class.get(ck, []):
+                self._run_chunk(ch, horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr,
+                                stats_ptr, status_ptr, lr32, decay, apply_decay, stream)
+            self._after_class(ck)
+        self._finish_collectives()
+        host = self.state.cpu().numpy()
+        return self._collect_stats(host, lr32)
+
+    def _run_chunk(self, ch, horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr, stats_ptr,
+                   status_ptr, lr32, decay, apply_decay, stream) -> None:
+        opt = self.opt
+        if True:
+            n = len(ch.blocks)
+            s_sums = sums_ptr + 8 * _lib.NSUMS * ch.slot0
+            s_flags = flags_ptr + 4 * ch.slot0
+            s_stats = stats_ptr + 4 * _lib.NSTATS * ch.slot0
+            self._mark("rebuild", True)
+            _lib.launch("muzo_rebuild_segments", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs, ch.rebuild_items,
+                keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, self.dist, ch.dtype_code,
+                normalize, inv_cs, s_sums, s_flags, stream)
+            self._mark("rebuild", False)
+            self._mark("normalize", True)
+            _lib.launch("muzo_ns_normalize", ch.norm_table.data_ptr(), n, ch.norm_items, s_sums, s_flags, stream)
+            self._mark("normalize", False)
+            buf = self.buffers[(ch.rows, ch.cols, ch.dtype_code)]
+            if ch.pad_views is not None:
+                buf.x_slot(0)[:n, :, : ch.cols].copy_(ch.pad_views[0])
+            self._mark("ns", True)
+            parity = ns_iterations(buf, n, opt.ns_steps, 0, status_ptr, stream)
+            self._mark("ns", False)
+            if ch.pad_views is not None:
+                ch.pad_views[0].copy_(buf.x_slot(parity)[:n, :, : ch.cols])
+            table, items = ch.apply_tables[parity if ch.pad_views is None else 0]
+            self._mark("apply", True)
+            _lib.launch("muzo_update_sumsq", table.data_ptr(), n, items, ch.scales.data_ptr(), s_sums,
+                                                  s_flags, stream)
+            _lib.launch("muzo_apply_update", table.data_ptr(), n, items, ch.dtype_code, ch.scales.data_ptr(), lr32,
+                float(opt.update_ratio_clip), apply_decay, decay, s_sums, s_flags, s_stats, stream)
+            self._mark("apply", False)
+
+    # hooks for the sharded (multi-GPU) engine
+    def _after_class(self, class_key) -> None:
+        pass
+
+    def _finish_collectives(self) -> None:
+        pass
+
+    def _collect_stats(self, host: np.ndarray, lr32: float) -> dict[int, dict[str, float]]:
+        n = max(self.n_slots, 1)
+        sums = host[: self.sums_bytes].view(np.float64).reshape(n, _lib.NSUMS)
+        flags = host[self.flags_off: self.flags_off + 4 * (n + 4)].view(np.int32)
+        stats = host[self.stats_off: self.stats_off + 4 * _lib.NSTATS * n].view(np.float32).reshape(n, _lib.NSTATS)
+        status = int(flags[n])
+        if status != 0:
+            raise _lib.MuzoError(f"Newton-Schulz GEMM reported status {status} (bounded wait expired)")
+        out: dict[int, dict[str, float]] = {}
+        lr = np.float32(lr32)
+        slot = 0
+        for ch in self.chunks:
+            for b in ch.blocks:
+                s = sums[slot]
+                st = stats[slot]
+                numel = float(b.numel)
+                zeroed = bool(st[_lib.STAT_ZEROED] != 0)
+                rms_w = np.float32(math.sqrt(s[_lib.SUM_W2] / numel))
+                denom = np.float32(rms_w + np.float32(1e-12))
+                if zeroed:
+                    update_rms, ratio = 0.0, 0.0
+                else:
+                    rms_u = np.float32(math.sqrt(s[_lib.SUM_U2_CLIPPED] / numel))
+                    update_rms_f = np.float32(rms_u * lr)
+                    update_rms = float(update_rms_f)
+                    ratio = float(np.float32(update_rms_f / denom))
+                out[b.index] = {
+                    "update_rms": update_rms,
+                    "ratio": ratio,
+                    "ratio_before": float(st[_lib.STAT_RATIO_BEFORE]),
+                    "clip": float(st[_lib.STAT_CLIP_FACTOR]),
+                    "zeroed": zeroed,
+                    "flags": int(flags[slot]),
+                }
+                slot += 1
+        return out

@@ -1,0 +1,164 @@
+"""Device helpers of QK-Clip: per-head max-logit kernels, the probe attention function that
+transformers calls during a probe forward, and the q/k row scaling."""
+
+from __future__ import annotations
+
+import contextvars
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_ACTIVE = contextvars.ContextVar("muzo_qk_controller", default=None)
+_REGISTERED = False
+
+
+def set_active_controller(ctrl):
+    return _ACTIVE.set(ctrl)
+
+
+def reset_active_controller(token) -> None:
+    _ACTIVE.reset(token)
+
+
+# ---------------------------------------------------------------- reductions
+
+
+def _check_cuda(t: torch.Tensor) -> None:
+    if t.device.type != "cuda":
+        raise ValueError("muzo_clip_b200 QK-Clip kernels run on CUDA tensors only")
+
+
+def logits_head_max(logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-head max over [B, H, Sq, Sk] logits and a validity word (0 when any logit is
+    non-finite), both on the device."""
+    _check_cuda(logits)
+    b, h, sq, sk = (int(v) for v in logits.shape)
+    out = torch.empty(h, dtype=torch.float32, device=logits.device)
+    valid = torch.empty(1, dtype=torch.int32, device=logits.device)
+    sb, sh, sqs, sks = (int(v) for v in logits.stride())
+    _lib.launch("muzo_logits_head_max", logits.data_ptr(), _lib.dtype_code(logits.dtype), b, h, sq, sk, sb, sh, sqs,
+                                      sks, out.data_ptr(), valid.data_ptr(), _lib.stream_ptr(logits.device))
+    return out, valid
+
+
+def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: bool,
+                attention_mask: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-head max of the eager pre-softmax logits of one attention call, from Q [B, Hq, Sq, D]
+    and K [B, Hkv, Sk, D] (any strides with D contiguous)."""
+    _check_cuda(query)
+    if attention_mask is not None and not _is_plain_causal(attention_mask, query.shape[2], key.shape[2]):
+        # an additive mask that is not the plain causal mask: reduce explicit logits
+        from torch.nn import functional as F  # noqa: F401  (kept local: rare path)
+
+        group = query.shape[1] // key.shape[1]
+        kr = key.repeat_interleave(group, dim=1)
+        logits = torch.matmul(query, kr.transpose(2, 3)) * scaling + attention_mask
+        return logits_head_max(logits)
+    q, k = query, key
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if k.stride(-1) != 1:
+        k = k.contiguous()
+    b, hq, sq, d = (int(v) for v in q.shape)
+    hkv, sk = int(k.shape[1]), int(k.shape[2])
+    out = torch.empty(hq, dtype=torch.float32, device=q.device)
+    valid = torch.empty(1, dtype=torch.int32, device=q.device)
+    _lib.launch("muzo_qk_max", q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), b, hq, hkv, sq, sk, d,
+                             q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+                             1 if causal else 0, float(scaling), out.data_ptr(), valid.data_ptr(),
+                             _lib.stream_ptr(q.device))
+    return out, valid
+
+
+def _is_plain_causal(mask: torch.Tensor, sq: int, sk: int) -> bool:
+    """True when an additive [B|1, 1|H, Sq, Sk] mask is 0 on and below the (end-aligned)
+    diagonal and a large negative value above it for every batch row."""
+    if mask.dtype == torch.bool:
+        return False
+    if mask.ndim != 4 or mask.shape[-2] != sq or mask.shape[-1] != sk:
+        return False
+    i = torch.arange(sq, device=mask.device)[:, None] + (sk - sq)
+    j = torch.arange(sk, device=mask.device)[None, :]
+    upper = j > i
+    m = mask.float()
+    lower_ok = bool((m[..., ~upper] == 0).all())
+    upper_ok = bool((m[..., upper] <= torch.finfo(torch.bfloat16).min / 2).all()) if upper.any() else True
+    return lower_ok and upper_ok
+
+
+def merge_max(running: torch.Tensor, new: torch.Tensor, valid: torch.Tensor | None) -> None:
+    """running = max(running, new) where ``valid`` is nonzero (device-side, no sync)."""
+    _lib.launch("muzo_max_merge", running.data_ptr(), new.data_ptr(), valid.data_ptr() if valid is not None else None,
+                                int(running.numel()), _lib.stream_ptr(running.device))
+
+
+def to_host(tensors: list[torch.Tensor]) -> list[np.ndarray]:
+    if not tensors:
+        return []
+    flat = torch.cat([t.reshape(-1) for t in tensors]).cpu().numpy()
+    out, off = [], 0
+    for t in tensors:
+        out.append(flat[off: off + t.numel()].copy())
+        off += t.numel()
+    return out
+
+
+# ---------------------------------------------------------------- scaling
+
+
+def pow_factors(gamma: np.ndarray, exponent: float, dtype: torch.dtype) -> np.ndarray:
+    """gamma ** exponent in fp32 (correctly rounded from float64), then rounded to ``dtype``
+    the way ``.to(dtype)`` does; returned as fp32 values."""
+    f = np.power(np.asarray(gamma, np.float64), float(exponent)).astype(np.float32)
+    return torch.from_numpy(f).to(dtype).float().numpy()
+
+
+def scale_rows(weight: torch.Tensor, groups: int, rows_per_group: int, factors: np.ndarray, mask: np.ndarray) -> None:
+    """Rows of group g of ``weight`` *= factors[g] where mask[g] (qk_clip.py:289-308)."""
+    _check_cuda(weight)
+    if not weight.is_contiguous():
+        raise ValueError("QK-Clip scaling expects contiguous projection weights")
+    dev = weight.device
+    payload = np.concatenate([np.asarray(factors, np.float32).view(np.uint8),
+                              np.asarray(mask, np.int32).view(np.uint8)])
+    buf = torch.from_numpy(payload).to(dev)
+    fptr = buf.data_ptr()
+    mptr = fptr + 4 * int(groups)
+    _lib.launch("muzo_qk_scale_rows", weight.data_ptr(), _lib.dtype_code(weight.dtype), int(groups), int(rows_per_group),
+                                    int(weight.shape[1]), fptr, mptr, _lib.stream_ptr(dev))
+
+
+# ---------------------------------------------------------------- probe attention
+
+
+def _probe_attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
+    """Attention function used during a probe forward: records the per-head max logit with the
+    kernel, then returns SDPA's output."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    ctrl = _ACTIVE.get()
+    if scaling is None:
+        scaling = query.shape[-1] ** -0.5
+    if ctrl is not None:
+        causal = bool(getattr(module, "is_causal", True)) and query.shape[2] > 1
+        mask = attention_mask if attention_mask is not None and attention_mask.ndim == 4 else None
+        ctrl.record_qk(module, query, key, float(scaling), causal if mask is None else True, mask)
+    return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
+                                  **kwargs)
+
+
+def ensure_probe_registered() -> str:
+    """Register the probe attention (with the eager mask format) with transformers once."""
+    global _REGISTERED
+    from .qk_clip import PROBE_ATTENTION
+
+    if not _REGISTERED:
+        from transformers import AttentionInterface
+        from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS, eager_mask
+
+        AttentionInterface.register(PROBE_ATTENTION, _probe_attention)
+        ALL_MASK_ATTENTION_FUNCTIONS.register(PROBE_ATTENTION, eager_mask)
+        _REGISTERED = True
+    return PROBE_ATTENTION

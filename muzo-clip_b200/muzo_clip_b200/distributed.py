@@ -1,0 +1,61 @@
+"""Sharded step over the ranks of a torch.distributed process group (one process per GPU).
+
+Every rank keeps a full replica of the selected weights. Perturbation needs no communication:
+the noise of a block is a pure function of (seed, name, shape, block index), so all ranks
+perturb their replicas identically. The step is partitioned: blocks are assigned to ranks by
+Newton-Schulz FLOPs (LPT greedy, identical on every rank); each rank rebuilds, orthogonalises
+and applies only its blocks, and after each shape class the owners broadcast the updated blocks
+with NCCL — asynchronously, on NCCL's stream, so the transfer of class c overlaps the GEMMs of
+class c + 1. Per-block statistics are combined with one small all-reduce.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ._engine import StepEngine
+
+
+class ShardedStepEngine(StepEngine):
+    def __init__(self, opt, process_group):
+        self.group = process_group
+        rank = dist.get_rank(process_group)
+        world = dist.get_world_size(process_group)
+        super().__init__(opt, rank=rank, world=world, process_group=process_group)
+        self._works: list = []
+        self._global_ranks = [dist.get_global_rank(process_group, r) if process_group is not None else r
+                              for r in range(world)] if process_group is not None else list(range(world))
+
+    def _after_class(self, class_key) -> None:
+        if self.world <= 1:
+            return
+        for b in self.blocks:
+            if (b.rows, b.cols, self._code(b)) != class_key:
+                continue
+            src = self._global_ranks[self.owner[b.index]]
+            self._works.append(dist.broadcast(b.tensor, src=src, group=self.group, async_op=True))
+
+    @staticmethod
+    def _code(b) -> int:
+        from . import _lib
+
+        return _lib.dtype_code(b.dtype)
+
+    def _finish_collectives(self) -> None:
+        works, self._works = self._works, []
+        for w in works:
+            w.wait()  # makes the current stream wait for NCCL's; no host block
+
+    def gather_stats(self, per_block: dict[int, dict]) -> dict[int, dict]:
+        """Combine the owners' per-block statistics on every rank (sum all-reduce)."""
+        n = len(self.blocks)
+        host = np.zeros((n, 3), dtype=np.float64)
+        for i, st in per_block.items():
+            host[i] = (st["update_rms"], st["ratio"], 1.0)
+        t = torch.from_numpy(host).to(self.device)
+        if self.world > 1:
+            dist.all_reduce(t, group=self.group)
+        host = t.cpu().tolist()
+        return {i: {"update_rms": row[0], "ratio": row[1]} for i, row in enumerate(host) if row[2] > 0}

@@ -1,0 +1,96 @@
+"""The C-ABI library loads, exports every declared symbol, and its host-side logic (block keys,
+launch planning) agrees with the oracle — no GPU needed."""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import re
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, ROOT
+
+import muzo_oracle as oracle
+
+
+def _declared_symbols() -> list[str]:
+    text = (ROOT / "include" / "muzo_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(muzo_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(ROOT / "muzo-clip_b200" / "muzo_clip_b200" / "libmuzo_b200.so"))
+    declared = _declared_symbols()
+    assert len(declared) >= 15
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    from muzo_clip_b200 import _lib
+
+    assert set(_declared_symbols()) == set(_lib.EXPORTED)
+    assert _lib.lib.muzo_abi_version() == 1
+
+
+def test_hash_known_answers_native_and_python():
+    from muzo_clip_b200 import _lib
+    from muzo_clip_b200.prng import hash64_seed
+
+    cases = json.loads((GOLDEN / "hash_kat.json").read_text())
+    assert cases
+    for c in cases:
+        key = c["key"]
+        assert hash64_seed(c["seed"], c["name"], tuple(c["shape"]), c["block"]) == key
+        assert oracle.hash64_seed(c["seed"], c["name"], tuple(c["shape"]), c["block"]) == key
+        assert _lib.hash64_seed_native(c["seed"], c["name"], tuple(c["shape"]), c["block"]) == key
+
+
+@pytest.mark.parametrize("numel", [1, 255, 256, 1000, 303104, 303105, 1 << 22, (1 << 29) + 1000, (1 << 31) + 64,
+                                   (1 << 33) + 12345])
+@pytest.mark.parametrize("dist", [0, 1])
+def test_native_planner_matches_oracle(numel, dist):
+    from muzo_clip_b200 import _lib
+
+    segs, total = _lib.plan_segments([numel], [4096], [8192], dist, 148, 2048)
+    launches = oracle.noise_launches(numel, 4 if dist == 0 else 1, 148, 2048)
+    assert len(segs) == len(launches)
+    items = 0
+    for s, l in zip(segs, launches):
+        assert int(s["elem_start"]) == l.start
+        assert int(s["numel"]) == l.count
+        assert int(s["threads"]) == l.threads
+        assert int(s["philox_offset"]) == l.offset
+        assert int(s["item_begin"]) == items
+        assert int(s["param"]) == 4096 and int(s["out"]) == 8192
+        trips = (l.count - 1) // (l.threads * 4) + 1
+        n = trips * (l.threads // 8)
+        items += (n + _lib.ITEMS_PER_CTA - 1) // _lib.ITEMS_PER_CTA * _lib.ITEMS_PER_CTA
+    assert total == items
+
+
+def test_linear_planner():
+    from muzo_clip_b200 import _lib
+
+    segs, total = _lib.plan_linear([10, 8192 * 1024 + 3, 1], [1, 2, 3], [4, 5, 6])
+    assert [int(s["numel"]) for s in segs] == [10, 8192 * 1024 + 3, 1]
+    assert [int(s["block_index"]) for s in segs] == [0, 1, 2]
+    per = [(n + 7) // 8 for n in (10, 8192 * 1024 + 3, 1)]
+    per = [(p + 1023) // 1024 * 1024 for p in per]
+    assert [int(s["item_begin"]) for s in segs] == [0, per[0], per[0] + per[1]]
+    assert total == sum(per)
+
+
+def test_status_strings_and_bad_args():
+    from muzo_clip_b200 import _lib
+
+    assert _lib.lib.muzo_status_string(0) == b"ok"
+    assert _lib.lib.muzo_status_string(3).startswith(b"pointer")
+    # null tables are rejected before anything touches a device
+    assert _lib.lib.muzo_perturb_segments(None, 1, 1024, None, 1, 0, 1.0, None) == 1
+    assert _lib.lib.muzo_ns_gemm(None, 8, 0, 0, None, 8, 0, 0, None, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, None, None) == 1
+    # unaligned leading dimension
+    assert _lib.lib.muzo_ns_gemm(16, 12, 0, 0, 16, 8, 0, 0, 16, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, None, None) == 3
