@@ -91,6 +91,7 @@ _SIGNATURES = {
     ),
     "muzo_logits_head_max": ([_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp], _i32),
     "muzo_max_merge": ([_vp, _vp, _vp, _i64, _vp], _i32),
+    "muzo_ns_normalize_noalloc": ([_vp, _vp, _vp, _i32, _i32, _vp, _vp], _i32),
 }
 
 for _name, (_args, _ret) in _SIGNATURES.items():
@@ -110,6 +111,7 @@ KERNELS_PER_CALL = {
     "muzo_fill_noise": 1, "muzo_perturb_segments": 1, "muzo_rebuild_segments": 1, "muzo_ns_prepare": 1,
     "muzo_ns_normalize": 1, "muzo_ns_gemm": 1, "muzo_update_sumsq": 1, "muzo_apply_update": 1,
     "muzo_qk_scale_rows": 1, "muzo_qk_max": 3, "muzo_logits_head_max": 3, "muzo_max_merge": 1,
+    "muzo_ns_normalize_noalloc": 3,
 }
 launch_count = 0
 
