@@ -40,6 +40,31 @@ __device__ __forceinline__ void noise8x4(uint64_t key, uint64_t t0, uint64_t wor
   }
 }
 
+// acc[j][k] += alpha * float(dtype(z[j][k])) for the noise of threads t0..t0+7 (trip `trip`),
+// one thread's Philox block at a time so only four noise values are live.
+template <int DIST, int PDTYPE>
+__device__ __forceinline__ void accumulate8x4(uint64_t key, uint64_t t0, uint64_t word_offset, uint64_t trip,
+                                              float alpha, float (&acc)[4][8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    curandStatePhilox4_32_10_t st;
+    curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
+    float z[4];
+    if (DIST == MUZO_NORMAL) {
+      float4 n = curand_normal4(&st);
+      z[0] = n.x; z[1] = n.y; z[2] = n.z; z[3] = n.w;
+    } else {
+      uint4 r = curand4(&st);
+      z[0] = (r.x & 1u) ? 1.0f : -1.0f;
+      z[1] = (r.y & 1u) ? 1.0f : -1.0f;
+      z[2] = (r.z & 1u) ? 1.0f : -1.0f;
+      z[3] = (r.w & 1u) ? 1.0f : -1.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j][k] = __fmaf_rn(alpha, round_to(z[j], PDTYPE), acc[j][k]);
+  }
+}
+
 __device__ __forceinline__ int elem_size(int dtype) { return dtype == MUZO_F32 ? 4 : 2; }
 
 __device__ __forceinline__ bool vec_ok(const void* base, int64_t elem_start, int dtype) {
@@ -58,8 +83,9 @@ struct SegView {
 };
 
 // Every CTA handles MUZO_ITEMS_PER_CTA consecutive items of exactly one segment.
-__device__ __forceinline__ SegView cta_segment(const muzo_segment* segs, int nsegs, int pdtype, int odtype) {
-  const int64_t item0 = static_cast<int64_t>(blockIdx.x) * MUZO_ITEMS_PER_CTA;
+__device__ __forceinline__ SegView cta_segment(const muzo_segment* segs, int nsegs, int pdtype, int odtype,
+                                               int64_t chunk = -1) {
+  const int64_t item0 = (chunk < 0 ? static_cast<int64_t>(blockIdx.x) : chunk) * MUZO_ITEMS_PER_CTA;
   const int s = find_segment(segs, nsegs, item0);
   const muzo_segment& g = segs[s];
   SegView v;
@@ -172,11 +198,12 @@ __device__ __forceinline__ void block_accumulate3(double a, double b, double c, 
 // M = sum_h alphas[h] * float(dtype(Z_h)) (h = age, newest first, as the reference walks
 // reversed(history)); M *= inv_coeff_sum; out = bf16(M). Also sums M^2, bf16(M)^2 and W^2.
 template <int DIST, int PDTYPE>
-__global__ void __launch_bounds__(kElemThreads)
-rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
-               const float* __restrict__ alphas, int horizon, int normalize, float inv_coeff_sum,
-               double* __restrict__ sums, int32_t* __restrict__ flags) {
-  const SegView sv = cta_segment(segs, nsegs, PDTYPE, MUZO_BF16);
+__device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ segs, int nsegs,
+                                              const uint64_t* __restrict__ keys, const float* __restrict__ alphas,
+                                              int horizon, int normalize, float inv_coeff_sum,
+                                              double* __restrict__ sums, int32_t* __restrict__ flags,
+                                              int64_t chunk) {
+  const SegView sv = cta_segment(segs, nsegs, PDTYPE, MUZO_BF16, chunk);
   const uint32_t octets = sv.threads / 8;
   const bool vec = vec_ok(sv.out, 0, MUZO_BF16) && vec_ok(sv.param, 0, PDTYPE);
   const uint64_t* bkeys = keys + static_cast<int64_t>(sv.block) * horizon;
@@ -195,15 +222,8 @@ rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[j][k] = 0.0f;
 #pragma unroll 1
-    for (int h = 0; h < horizon; ++h) {
-      float z[4][8];
-      noise8x4<DIST>(bkeys[h], 8ull * oct, sv.philox_offset, trip, z);
-      const float a = alphas[h];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[j][k] = __fmaf_rn(a, round_to(z[j][k], PDTYPE), acc[j][k]);
-    }
+    for (int h = 0; h < horizon; ++h)
+      accumulate8x4<DIST, PDTYPE>(bkeys[h], 8ull * oct, sv.philox_offset, trip, alphas[h], acc);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
@@ -236,6 +256,17 @@ rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
   double* bs = sums + static_cast<int64_t>(sv.block) * MUZO_NSUMS;
   block_accumulate3(m2, x2, w2, bs + MUZO_SUM_M2, bs + MUZO_SUM_X2, bs + MUZO_SUM_W2);
   if (!finite) atomicOr(flags + sv.block, MUZO_FLAG_NONFINITE_INPUT);
+}
+
+template <int DIST, int PDTYPE>
+__global__ void __launch_bounds__(kElemThreads, 2)
+rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
+               const float* __restrict__ alphas, int horizon, int normalize, float inv_coeff_sum,
+               double* __restrict__ sums, int32_t* __restrict__ flags, int64_t nchunks) {
+  // a CTA walks chunks blockIdx.x, blockIdx.x + gridDim.x, ... (grid may be smaller than the
+  // number of chunks, e.g. one CTA per SM next to a concurrently running GEMM)
+  for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x)
+    rebuild_chunk<DIST, PDTYPE>(segs, nsegs, keys, alphas, horizon, normalize, inv_coeff_sum, sums, flags, chunk);
 }
 
 bool valid_dtype(int d) { return d == MUZO_F32 || d == MUZO_BF16 || d == MUZO_F16; }
@@ -303,23 +334,25 @@ int muzo_perturb_segments(const muzo_segment* d_segs, int nsegs, int64_t total_i
 int muzo_rebuild_segments(const muzo_segment* d_segs, int nsegs, int64_t total_items,
                           const uint64_t* d_keys, const float* d_alphas, int horizon, int dist,
                           int param_dtype, int normalize, float inv_coeff_sum, double* d_sums,
-                          int32_t* d_flags, void* stream) {
+                          int32_t* d_flags, int max_ctas, void* stream) {
   if (nsegs == 0 || total_items == 0) return MUZO_OK;
   int st = check_table(d_segs, nsegs, total_items);
   if (st != MUZO_OK) return st;
   if (d_keys == nullptr || d_alphas == nullptr || d_sums == nullptr || d_flags == nullptr ||
       horizon <= 0 || (dist != MUZO_NORMAL && dist != MUZO_RADEMACHER))
     return MUZO_ERR_ARG;
-  const dim3 grid(static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA));
+  const int64_t nchunks = total_items / MUZO_ITEMS_PER_CTA;
+  const int64_t ctas = (max_ctas > 0 && max_ctas < nchunks) ? max_ctas : nchunks;
+  const dim3 grid(static_cast<unsigned>(ctas));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = dispatch_dtype(param_dtype, [&](auto d) {
     constexpr int D = decltype(d)::value;
     if (dist == MUZO_NORMAL)
       rebuild_kernel<MUZO_NORMAL, D><<<grid, kElemThreads, 0, s>>>(
-          d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags);
+          d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags, nchunks);
     else
       rebuild_kernel<MUZO_RADEMACHER, D><<<grid, kElemThreads, 0, s>>>(
-          d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags);
+          d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags, nchunks);
   });
   if (st != MUZO_OK) return st;
   return launch_status();

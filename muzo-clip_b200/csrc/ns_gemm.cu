@@ -153,6 +153,8 @@ __host__ __device__ constexpr uint32_t make_idesc(int m, int n, bool a_mn, bool 
 struct GemmArgs {
   int64_t m, n, k, batch;
   int tiles_m, tiles_n;
+  int sym;                 // symmetric output: only tiles meeting the upper triangle, mirrored
+  int64_t tiles_per_batch;
   int64_t num_tiles;
   int num_kb;
   __nv_bfloat16* d;
@@ -166,6 +168,7 @@ template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, int64_t b, int64_t row, int64_t col0,
                                                const uint32_t (&acc)[32]) {
   if (row >= g.m || col0 >= g.n) return;
+  if (g.sym && col0 + 31 < row) return;  // strictly below the diagonal: written by the mirror
   const int64_t base = b * g.d_bs + row * g.ldd + col0;
   float o[32];
   if (EPI == MUZO_EPI_STORE) {
@@ -198,6 +201,23 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, int64_t b, int
       }
     }
   }
+  if (g.sym) {
+    // mirror (j, row) of every element with j >= row: for a fixed j the 32 lanes of a warp hold
+    // 32 consecutive rows, so each mirrored store is one contiguous 64-byte run
+    const int64_t mbase = b * g.d_bs + row;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int64_t j = col0 + i;
+      if (j < g.n && j >= row) g.d[mbase + j * g.ldd] = __float2bfloat16_rn(o[i]);
+    }
+    if (col0 < row) {  // chunk crosses the diagonal: direct stores of its upper part only
+      for (int i = 0; i < 32; ++i) {
+        const int64_t j = col0 + i;
+        if (j < g.n && j >= row) g.d[base + i] = __float2bfloat16_rn(o[i]);
+      }
+      return;
+    }
+  }
   if (col0 + 32 <= g.n) {
     uint4* dp = reinterpret_cast<uint4*>(g.d + base);
 #pragma unroll
@@ -214,12 +234,25 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, int64_t b, int
   }
 }
 
+// Tile t -> (batch, tile row, tile column). Symmetric outputs enumerate, per tile row tm, only
+// the columns tn >= tm * BM / BN (tiles that hold an element on or above the diagonal).
 __device__ __forceinline__ void tile_coords(const GemmArgs& g, int64_t t, int64_t& b, int& tm, int& tn) {
-  const int64_t per_batch = static_cast<int64_t>(g.tiles_m) * g.tiles_n;
-  b = t / per_batch;
-  const int64_t r = t - b * per_batch;
-  tm = static_cast<int>(r / g.tiles_n);
-  tn = static_cast<int>(r - static_cast<int64_t>(tm) * g.tiles_n);
+  b = t / g.tiles_per_batch;
+  int64_t r = t - b * g.tiles_per_batch;
+  if (!g.sym) {
+    tm = static_cast<int>(r / g.tiles_n);
+    tn = static_cast<int>(r - static_cast<int64_t>(tm) * g.tiles_n);
+    return;
+  }
+  int row = 0;
+  while (true) {
+    const int64_t width = g.tiles_n - (row * BM) / BN;
+    if (r < width) break;
+    r -= width;
+    ++row;
+  }
+  tm = row;
+  tn = static_cast<int>((row * BM) / BN + r);
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -463,11 +496,12 @@ extern "C" {
 int muzo_ns_gemm(const void* a, int64_t lda, int64_t a_batch_stride, int a_mn, const void* b, int64_t ldb,
                  int64_t b_batch_stride, int b_mn, void* d, int64_t ldd, int64_t d_batch_stride,
                  const void* e, int epilogue, float c1, float c2, int64_t m, int64_t n, int64_t k,
-                 int64_t batch, int32_t* d_status, void* stream) {
+                 int64_t batch, int symmetric, int32_t* d_status, void* stream) {
   if (a == nullptr || b == nullptr || d == nullptr || m <= 0 || n <= 0 || k <= 0 || batch <= 0)
     return MUZO_ERR_ARG;
   if (epilogue != MUZO_EPI_STORE && e == nullptr) return MUZO_ERR_ARG;
   if (epilogue < MUZO_EPI_STORE || epilogue > MUZO_EPI_UPDATE) return MUZO_ERR_ARG;
+  if (symmetric && (m != n || epilogue == MUZO_EPI_UPDATE)) return MUZO_ERR_ARG;
   if (lda % 8 || ldb % 8 || ldd % 8 || a_batch_stride % 8 || b_batch_stride % 8 || d_batch_stride % 8 ||
       !aligned16h(a) || !aligned16h(b) || !aligned16h(d) || (e && !aligned16h(e)))
     return MUZO_ERR_ALIGN;
@@ -488,7 +522,14 @@ int muzo_ns_gemm(const void* a, int64_t lda, int64_t a_batch_stride, int a_mn, c
   g.m = m; g.n = n; g.k = k; g.batch = batch;
   g.tiles_m = static_cast<int>((m + BM - 1) / BM);
   g.tiles_n = static_cast<int>((n + BN - 1) / BN);
-  g.num_tiles = static_cast<int64_t>(g.tiles_m) * g.tiles_n * batch;
+  g.sym = symmetric ? 1 : 0;
+  if (g.sym) {
+    g.tiles_per_batch = 0;
+    for (int tm = 0; tm < g.tiles_m; ++tm) g.tiles_per_batch += g.tiles_n - (tm * BM) / BN;
+  } else {
+    g.tiles_per_batch = static_cast<int64_t>(g.tiles_m) * g.tiles_n;
+  }
+  g.num_tiles = g.tiles_per_batch * batch;
   g.num_kb = static_cast<int>((k + BK - 1) / BK);
   g.d = static_cast<__nv_bfloat16*>(d);
   g.ldd = ldd;

@@ -10,6 +10,7 @@ apply, and the step statistics come back in one device-to-host copy.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Sequence
 
@@ -17,7 +18,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .newton_schulz import NSBuffers, allocate_ns_buffers, ns_iterations
+from .newton_schulz import NSBuffers, ns_buffers_in, ns_iterations, ns_workspace_bytes
 from .prng import hash64_seed, iter_param_blocks
 
 DEFAULT_WORKSPACE_BYTES = 16 << 30
@@ -65,6 +66,7 @@ class Chunk:
     apply_tables: dict[int, tuple[torch.Tensor, int]] = field(default_factory=dict)  # by parity
     scales: torch.Tensor | None = None
     pad_views: list[torch.Tensor] | None = None
+    buf: NSBuffers | None = None
 
 
 class _Uploader:
@@ -144,6 +146,9 @@ class StepEngine:
         self.owned = [b for b in blocks if self.owner[b.index] == rank]
         self._step_ready = False
         self._phase_events = None
+        # rebuild of batch i+1 on a side stream (one CTA per SM) while batch i is on the tensor
+        # cores; off by default: the GEMMs already run at the power cap
+        self.overlap = os.environ.get("MUZO_OVERLAP_REBUILD", "0") == "1"
         horizon = max(opt.horizon, 1)
         self.uploader = _Uploader(self.device, 8 * (len(blocks) * (horizon + 1) + 64))
 
@@ -206,65 +211,71 @@ class StepEngine:
         return max(budget, 1)
 
     def _build_step(self) -> None:
+        """Plan the step: shape classes in a global order (cheapest rebuild first, identical on
+        every rank), batches of owned blocks per class sized to half the workspace budget, and
+        two workspace slots used alternately so that the rebuild of batch i+1 (side stream) can
+        run while batch i is on the tensor cores."""
         opt = self.opt
-        # classes in first-appearance order over ALL blocks, so every rank walks them alike
-        self.class_order: list[tuple[int, int, int]] = []
+        first_seen: dict[tuple[int, int, int], int] = {}
         for b in self.blocks:
-            ck = (b.rows, b.cols, _lib.dtype_code(b.dtype))
-            if ck not in self.class_order:
-                self.class_order.append(ck)
-        classes: dict[tuple[int, int, int], list[Block]] = {ck: [] for ck in self.class_order}
+            first_seen.setdefault((b.rows, b.cols, _lib.dtype_code(b.dtype)), len(first_seen))
+        self.class_order = sorted(first_seen, key=lambda ck: (ck[0] * ck[1], first_seen[ck]))
+        owned_by_class: dict[tuple[int, int, int], list[Block]] = {ck: [] for ck in self.class_order}
         for b in self.owned:
-            classes[(b.rows, b.cols, _lib.dtype_code(b.dtype))].append(b)
-        classes = {ck: v for ck, v in classes.items() if v}
-        budget = self._workspace_budget()
-        per_block_max = 0
+            owned_by_class[(b.rows, b.cols, _lib.dtype_code(b.dtype))].append(b)
+        slot_budget = max(self._workspace_budget() // 2, 1)
         plans = []
-        for (rows, cols, code), blks in classes.items():
-            m = min(rows, cols)
-            per_block = 2 * rows * ((cols + 7) // 8 * 8) * 2 + 2 * m * ((m + 7) // 8 * 8) * 2
-            chunk = max(1, min(len(blks), budget // max(per_block, 1)))
-            plans.append((rows, cols, code, blks, chunk))
-            per_block_max = max(per_block_max, per_block * chunk)
+        for ck in self.class_order:
+            blks = owned_by_class[ck]
+            if not blks:
+                continue
+            rows, cols, _ = ck
+            per_block = ns_workspace_bytes(rows, cols, 1)
+            cap = max(1, min(len(blks), slot_budget // per_block))
+            nchunks = -(-len(blks) // cap)
+            size = -(-len(blks) // nchunks)
+            for start in range(0, len(blks), size):
+                plans.append((ck, blks[start:start + size]))
+        slot_bytes = max((ns_workspace_bytes(ck[0], ck[1], len(part)) for ck, part in plans), default=256)
+        nslots = 2 if len(plans) > 1 else 1
+        self.slots = [torch.empty(slot_bytes, dtype=torch.uint8, device=self.device) for _ in range(nslots)]
         self.chunks: list[Chunk] = []
-        self.buffers: dict[tuple[int, int], NSBuffers] = {}
-        slot = 0
-        for rows, cols, code, blks, chunk in plans:
-            buf = allocate_ns_buffers(rows, cols, chunk, self.device)
-            self.buffers[(rows, cols, code)] = buf
-            for start in range(0, len(blks), chunk):
-                part = blks[start:start + chunk]
-                n = len(part)
-                dense = buf.ld == cols
-                # rebuild and normalise write X0 densely; padded layouts go through a staging copy
-                if dense:
-                    x0_ptrs = [buf.x_slot(0)[i].data_ptr() for i in range(n)]
-                    pad_views = None
-                else:
-                    stage = torch.empty((n, rows, cols), dtype=torch.bfloat16, device=self.device)
-                    x0_ptrs = [stage[i].data_ptr() for i in range(n)]
-                    pad_views = [stage]
-                rsegs, rtot = _lib.plan_segments([b.numel for b in part], [b.tensor.data_ptr() for b in part],
-                                                 x0_ptrs, self.dist, self.sms, self.max_thr)
-                nsegs, ntot = _lib.plan_linear([b.numel for b in part], x0_ptrs, x0_ptrs)
-                ch = Chunk(part, rows, cols, code, slot, _lib.to_device_table(rsegs, self.device), len(rsegs),
-                           rtot, _lib.to_device_table(nsegs, self.device), ntot, pad_views=pad_views)
-                for parity in (0, 1):
-                    xs = buf.x_slot(parity)
-                    outs = [xs[i].data_ptr() for i in range(n)] if dense else [stage[i].data_ptr() for i in range(n)]
-                    asegs, atot = _lib.plan_linear([b.numel for b in part], [b.tensor.data_ptr() for b in part], outs)
-                    ch.apply_tables[parity] = (_lib.to_device_table(asegs, self.device), atot)
-                scales = np.asarray([math.sqrt(max(b.rows, b.cols)) * opt.muon_scale for b in part], dtype=np.float32)
-                ch.scales = torch.from_numpy(scales).to(self.device)
-                self.chunks.append(ch)
-                slot += n
-        self.n_slots = slot
+        stat_slot = 0
+        for i, ((rows, cols, code), part) in enumerate(plans):
+            n = len(part)
+            buf = ns_buffers_in(self.slots[i % nslots], rows, cols, n)
+            dense = buf.ld == cols
+            # rebuild and normalise write X0 densely; padded layouts go through a staging copy
+            if dense:
+                x0_ptrs = [buf.x_slot(0)[j].data_ptr() for j in range(n)]
+                pad_views = None
+            else:
+                stage = torch.empty((n, rows, cols), dtype=torch.bfloat16, device=self.device)
+                x0_ptrs = [stage[j].data_ptr() for j in range(n)]
+                pad_views = [stage]
+            rsegs, rtot = _lib.plan_segments([b.numel for b in part], [b.tensor.data_ptr() for b in part],
+                                             x0_ptrs, self.dist, self.sms, self.max_thr)
+            nsegs, ntot = _lib.plan_linear([b.numel for b in part], x0_ptrs, x0_ptrs)
+            ch = Chunk(part, rows, cols, code, stat_slot, _lib.to_device_table(rsegs, self.device), len(rsegs), rtot,
+                       _lib.to_device_table(nsegs, self.device), ntot, pad_views=pad_views)
+            ch.buf = buf
+            for parity in (0, 1):
+                xs = buf.x_slot(parity)
+                outs = [xs[j].data_ptr() for j in range(n)] if dense else x0_ptrs
+                asegs, atot = _lib.plan_linear([b.numel for b in part], [b.tensor.data_ptr() for b in part], outs)
+                ch.apply_tables[parity] = (_lib.to_device_table(asegs, self.device), atot)
+            scales = np.asarray([math.sqrt(max(b.rows, b.cols)) * opt.muon_scale for b in part], dtype=np.float32)
+            ch.scales = torch.from_numpy(scales).to(self.device)
+            self.chunks.append(ch)
+            stat_slot += n
+        self.n_slots = stat_slot
+        self.side_stream = torch.cuda.Stream(self.device)
         # one zeroed device buffer per step: sums (f64), flags + status (i32), stats (f32)
-        self.sums_bytes = 8 * _lib.NSUMS * max(slot, 1)
+        self.sums_bytes = 8 * _lib.NSUMS * max(stat_slot, 1)
         self.flags_off = self.sums_bytes
-        self.stats_off = self.flags_off + 4 * (max(slot, 1) + 4)
+        self.stats_off = self.flags_off + 4 * (max(stat_slot, 1) + 4)
         self.stats_off = (self.stats_off + 15) // 16 * 16
-        self.state_bytes = self.stats_off + 4 * _lib.NSTATS * max(slot, 1)
+        self.state_bytes = self.stats_off + 4 * _lib.NSTATS * max(stat_slot, 1)
         self.state = torch.zeros(self.state_bytes, dtype=torch.uint8, device=self.device)
         self._step_ready = True
 
@@ -282,12 +293,12 @@ class StepEngine:
         finally:
             self._phase_events = None
 
-    def _mark(self, phase: str, start: bool) -> None:
+    def _mark(self, phase: str, start: bool, stream=None) -> None:
         ev_map = getattr(self, "_phase_events", None)
         if ev_map is None:
             return
         ev = torch.cuda.Event(enable_timing=True)
-        ev.record(torch.cuda.current_stream(self.device))
+        ev.record(stream if stream is not None else torch.cuda.current_stream(self.device))
         if start:
             ev_map.setdefault(phase, []).append([ev, None])
         else:
@@ -328,49 +339,84 @@ class StepEngine:
         lr32 = float(np.float32(lr))
         decay = float(np.float32(1.0 - lr * opt.weight_decay))
         apply_decay = 1 if opt.weight_decay else 0
-        chunks_by_class: dict[tuple[int, int, int], list[Chunk]] = {}
-        for ch in self.chunks:
-            chunks_by_class.setdefault((ch.rows, ch.cols, ch.dtype_code), []).append(ch)
-        for ck in self.class_order:
-            for ch in chunks_by_class.get(ck, []):
-                self._run_chunk(ch, horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr,
-                                stats_ptr, status_ptr, lr32, decay, apply_decay, stream)
-            self._after_class(ck)
+        compute = torch.cuda.current_stream(self.device)
+        side = self.side_stream if self.overlap else compute
+        inputs_ready = torch.cuda.Event()
+        inputs_ready.record(compute)
+        side.wait_event(inputs_ready)
+        done: list[torch.cuda.Event] = []
+        args = (horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr, stats_ptr, status_ptr, lr32,
+                decay, apply_decay)
+        next_class = 0
+        for i, ch in enumerate(self.chunks):
+            # rebuild + normalise on the side stream once the slot's previous user has finished
+            if i >= 2:
+                side.wait_event(done[i - 2])
+            self._prepare_chunk(ch, side, *args)
+            ready = torch.cuda.Event()
+            ready.record(side)
+            compute.wait_event(ready)
+            self._finish_chunk(ch, compute, *args)
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            done.append(ev)
+            ck = (ch.rows, ch.cols, ch.dtype_code)
+            last_of_class = i + 1 == len(self.chunks) or (self.chunks[i + 1].rows, self.chunks[i + 1].cols,
+                                                          self.chunks[i + 1].dtype_code) != ck
+            if last_of_class:
+                # collectives run class by class in the global order on every rank, including
+                # classes this rank owns nothing of
+                while next_class < len(self.class_order):
+                    cur = self.class_order[next_class]
+                    next_class += 1
+                    self._after_class(cur)
+                    if cur == ck:
+                        break
+        while next_class < len(self.class_order):
+            self._after_class(self.class_order[next_class])
+            next_class += 1
         self._finish_collectives()
         host = self.state.cpu().numpy()
         return self._collect_stats(host, lr32)
 
-    def _run_chunk(self, ch, horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr, stats_ptr,
-                   status_ptr, lr32, decay, apply_decay, stream) -> None:
+    def _prepare_chunk(self, ch, stream, horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr,
+                       stats_ptr, status_ptr, lr32, decay, apply_decay) -> None:
+        sp = stream.cuda_stream
+        n = len(ch.blocks)
+        s_sums = sums_ptr + 8 * _lib.NSUMS * ch.slot0
+        s_flags = flags_ptr + 4 * ch.slot0
+        self._mark("rebuild", True, stream)
+        _lib.launch("muzo_rebuild_segments", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs, ch.rebuild_items,
+                    keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, self.dist, ch.dtype_code, normalize,
+                    inv_cs, s_sums, s_flags, self.sms if self.overlap else 0, sp)
+        self._mark("rebuild", False, stream)
+        self._mark("normalize", True, stream)
+        _lib.launch("muzo_ns_normalize", ch.norm_table.data_ptr(), n, ch.norm_items, s_sums, s_flags, sp)
+        self._mark("normalize", False, stream)
+        if ch.pad_views is not None:
+            with torch.cuda.stream(stream):
+                ch.buf.x_slot(0)[:n, :, : ch.cols].copy_(ch.pad_views[0])
+
+    def _finish_chunk(self, ch, stream, horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr,
+                      stats_ptr, status_ptr, lr32, decay, apply_decay) -> None:
         opt = self.opt
-        if True:
-            n = len(ch.blocks)
-            s_sums = sums_ptr + 8 * _lib.NSUMS * ch.slot0
-            s_flags = flags_ptr + 4 * ch.slot0
-            s_stats = stats_ptr + 4 * _lib.NSTATS * ch.slot0
-            self._mark("rebuild", True)
-            _lib.launch("muzo_rebuild_segments", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs, ch.rebuild_items,
-                keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, self.dist, ch.dtype_code,
-                normalize, inv_cs, s_sums, s_flags, stream)
-            self._mark("rebuild", False)
-            self._mark("normalize", True)
-            _lib.launch("muzo_ns_normalize", ch.norm_table.data_ptr(), n, ch.norm_items, s_sums, s_flags, stream)
-            self._mark("normalize", False)
-            buf = self.buffers[(ch.rows, ch.cols, ch.dtype_code)]
-            if ch.pad_views is not None:
-                buf.x_slot(0)[:n, :, : ch.cols].copy_(ch.pad_views[0])
-            self._mark("ns", True)
-            parity = ns_iterations(buf, n, opt.ns_steps, 0, status_ptr, stream)
-            self._mark("ns", False)
-            if ch.pad_views is not None:
-                ch.pad_views[0].copy_(buf.x_slot(parity)[:n, :, : ch.cols])
-            table, items = ch.apply_tables[parity if ch.pad_views is None else 0]
-            self._mark("apply", True)
-            _lib.launch("muzo_update_sumsq", table.data_ptr(), n, items, ch.scales.data_ptr(), s_sums,
-                                                  s_flags, stream)
-            _lib.launch("muzo_apply_update", table.data_ptr(), n, items, ch.dtype_code, ch.scales.data_ptr(), lr32,
-                float(opt.update_ratio_clip), apply_decay, decay, s_sums, s_flags, s_stats, stream)
-            self._mark("apply", False)
+        sp = stream.cuda_stream
+        n = len(ch.blocks)
+        s_sums = sums_ptr + 8 * _lib.NSUMS * ch.slot0
+        s_flags = flags_ptr + 4 * ch.slot0
+        s_stats = stats_ptr + 4 * _lib.NSTATS * ch.slot0
+        self._mark("ns", True, stream)
+        parity = ns_iterations(ch.buf, n, opt.ns_steps, 0, status_ptr, sp)
+        self._mark("ns", False, stream)
+        if ch.pad_views is not None:
+            with torch.cuda.stream(stream):
+                ch.pad_views[0].copy_(ch.buf.x_slot(parity)[:n, :, : ch.cols])
+        table, items = ch.apply_tables[parity if ch.pad_views is None else 0]
+        self._mark("apply", True, stream)
+        _lib.launch("muzo_update_sumsq", table.data_ptr(), n, items, ch.scales.data_ptr(), s_sums, s_flags, sp)
+        _lib.launch("muzo_apply_update", table.data_ptr(), n, items, ch.dtype_code, ch.scales.data_ptr(), lr32,
+                    float(opt.update_ratio_clip), apply_decay, decay, s_sums, s_flags, s_stats, sp)
+        self._mark("apply", False, stream)
 
     # hooks for the sharded (multi-GPU) engine
     def _after_class(self, class_key) -> None:

@@ -68,14 +68,14 @@ _SIGNATURES = {
     "muzo_fill_noise": ([_vp, _i32, _i64, _u64, _i32, _i32, _vp], _i32),
     "muzo_perturb_segments": ([_vp, _i32, _i64, _vp, _i32, _i32, _f32, _vp], _i32),
     "muzo_rebuild_segments": (
-        [_vp, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp],
+        [_vp, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _vp],
         _i32,
     ),
     "muzo_ns_prepare": ([_vp, _i32, _i64, _i32, _vp, _vp, _vp], _i32),
     "muzo_ns_normalize": ([_vp, _i32, _i64, _vp, _vp, _vp], _i32),
     "muzo_ns_gemm": (
         [_vp, _i64, _i64, _i32, _vp, _i64, _i64, _i32, _vp, _i64, _i64, _vp, _i32, _f32, _f32,
-         _i64, _i64, _i64, _i64, _vp, _vp],
+         _i64, _i64, _i64, _i64, _i32, _vp, _vp],
         _i32,
     ),
     "muzo_update_sumsq": ([_vp, _i32, _i64, _vp, _vp, _vp, _vp], _i32),

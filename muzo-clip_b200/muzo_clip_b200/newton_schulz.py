@@ -52,6 +52,33 @@ class NSBuffers:
         return self.x[parity]
 
 
+def _align256(v: int) -> int:
+    return (v + 255) // 256 * 256
+
+
+def ns_workspace_bytes(rows: int, cols: int, batch: int) -> int:
+    """Bytes of the workspace of ``batch`` rows x cols matrices (see NSBuffers)."""
+    ld, m = _round8(cols), min(rows, cols)
+    ldm = _round8(m)
+    return _align256(2 * batch * rows * ld * 2) + 2 * _align256(batch * m * ldm * 2)
+
+
+def ns_buffers_in(raw: torch.Tensor, rows: int, cols: int, batch: int) -> NSBuffers:
+    """NSBuffers carved out of a flat uint8 device buffer of at least ns_workspace_bytes."""
+    ld, m = _round8(cols), min(rows, cols)
+    ldm = _round8(m)
+    xb = 2 * batch * rows * ld * 2
+    mb = batch * m * ldm * 2
+    off_a = _align256(xb)
+    off_b = off_a + _align256(mb)
+    if raw.numel() < off_b + mb:
+        raise ValueError("workspace too small")
+    x = raw[:xb].view(torch.bfloat16).view(2, batch, rows, ld)
+    a = raw[off_a:off_a + mb].view(torch.bfloat16).view(batch, m, ldm)
+    b = raw[off_b:off_b + mb].view(torch.bfloat16).view(batch, m, ldm)
+    return NSBuffers(rows, cols, batch, ld, ldm, x, a, b)
+
+
 def allocate_ns_buffers(rows: int, cols: int, batch: int, device: torch.device) -> NSBuffers:
     ld = _round8(cols)
     m = min(rows, cols)
@@ -63,13 +90,13 @@ def allocate_ns_buffers(rows: int, cols: int, batch: int, device: torch.device) 
 
 
 def _gemm(a, lda, abs_, a_mn, b, ldb, bbs, b_mn, d, ldd, dbs, e, epi, c1, c2, m, n, k, batch,
-          status, stream) -> None:
-    _lib.launch("muzo_ns_gemm", a, lda, abs_, a_mn, b, ldb, bbs, b_mn, d, ldd, dbs, e, epi,
-                              float(c1), float(c2), m, n, k, batch, status, stream)
+          status, stream, symmetric: int = 0) -> None:
+    _lib.launch("muzo_ns_gemm", a, lda, abs_, a_mn, b, ldb, bbs, b_mn, d, ldd, dbs, e, epi, float(c1), float(c2),
+                m, n, k, batch, symmetric, status, stream)
 
 
 def ns_iterations(buf: NSBuffers, batch: int, steps: int, start_parity: int, status_ptr: int,
-                  stream: int) -> int:
+                  stream: int, symmetric: int = 1) -> int:
     """Run ``steps`` quintic iterations on the first ``batch`` matrices; return the parity of the
     buffer that holds the result."""
 
@@ -85,17 +112,19 @@ def ns_iterations(buf: NSBuffers, batch: int, steps: int, start_parity: int, sta
     for _ in range(int(steps)):
         px = buf.x_slot(parity).data_ptr()
         py = buf.x_slot(parity ^ 1).data_ptr()
+        # A = X X^T and B = b A + c A A are symmetric: only their upper-triangle tiles are
+        # computed and mirrored
         if not tall:
             # A = X X^T: both operands are X's rows (K = cols contiguous)
             _gemm(px, ld, x_bs, 0, px, ld, x_bs, 0, pa, ldm, m_bs, None, _lib.EPI_STORE, 0.0, 0.0,
-                  m, m, cols, batch, status_ptr, stream)
+                  m, m, cols, batch, status_ptr, stream, symmetric)
         else:
             # X = G^T: A = G^T G reads G with M and N contiguous (MN-major), K = rows
             _gemm(px, ld, x_bs, 1, px, ld, x_bs, 1, pa, ldm, m_bs, None, _lib.EPI_STORE, 0.0, 0.0,
-                  m, m, rows, batch, status_ptr, stream)
+                  m, m, rows, batch, status_ptr, stream, symmetric)
         # B = b A + c (A @ A): second operand A[k][n] is N-contiguous (MN-major)
         _gemm(pa, ldm, m_bs, 0, pa, ldm, m_bs, 1, pb, ldm, m_bs, pa, _lib.EPI_POLY, b_c, c_c,
-              m, m, m, batch, status_ptr, stream)
+              m, m, m, batch, status_ptr, stream, symmetric)
         if not tall:
             # X' = a X + B @ X: X[k][n] is N-contiguous
             _gemm(pb, ldm, m_bs, 0, px, ld, x_bs, 1, py, ld, x_bs, px, _lib.EPI_UPDATE, a_c, 0.0,

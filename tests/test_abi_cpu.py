@@ -91,6 +91,6 @@ def test_status_strings_and_bad_args():
     assert _lib.lib.muzo_status_string(3).startswith(b"pointer")
     # null tables are rejected before anything touches a device
     assert _lib.lib.muzo_perturb_segments(None, 1, 1024, None, 1, 0, 1.0, None) == 1
-    assert _lib.lib.muzo_ns_gemm(None, 8, 0, 0, None, 8, 0, 0, None, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, None, None) == 1
+    assert _lib.lib.muzo_ns_gemm(None, 8, 0, 0, None, 8, 0, 0, None, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None) == 1
     # unaligned leading dimension
-    assert _lib.lib.muzo_ns_gemm(16, 12, 0, 0, 16, 8, 0, 0, 16, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, None, None) == 3
+    assert _lib.lib.muzo_ns_gemm(16, 12, 0, 0, 16, 8, 0, 0, 16, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None) == 3

@@ -1,0 +1,118 @@
+"""Host logic of the sharded step on two gloo ranks (CPU, no GPU).
+
+Covers: the LPT ownership is identical on every rank; owners' updated blocks reach every rank
+through the class-by-class broadcasts; per-block statistics combine to the same StepStats on all
+ranks; the SPSA losses are averaged over the group so every rank derives the same projection.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class _Block:
+    def __init__(self, index, rows, cols, tensor):
+        self.index, self.rows, self.cols, self.tensor, self.dtype = index, rows, cols, tensor, tensor.dtype
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from muzo_clip_b200._engine import ns_flops, partition_blocks
+        from muzo_clip_b200.distributed import ShardedStepEngine
+
+        shapes = [(64, 32), (16, 32), (16, 32), (64, 32), (96, 32), (96, 32), (32, 96)] * 3
+        blocks = [_Block(i, r, c, torch.full((r, c), -1.0)) for i, (r, c) in enumerate(shapes)]
+        owner = partition_blocks([ns_flops(r, c, 5) for r, c in shapes], world)
+
+        class Fake:  # the collective parts of ShardedStepEngine on CPU tensors
+            _after_class = ShardedStepEngine._after_class
+            _finish_collectives = ShardedStepEngine._finish_collectives
+            gather_stats = ShardedStepEngine.gather_stats
+            _code = staticmethod(ShardedStepEngine._code)
+
+        eng = Fake()
+        eng.blocks, eng.owner, eng.world, eng.group = blocks, owner, world, dist.group.WORLD
+        eng._works, eng._global_ranks, eng.device = [], list(range(world)), torch.device("cpu")
+        # owners "update" their blocks; everyone else holds stale values
+        for b in blocks:
+            if owner[b.index] == rank:
+                b.tensor.fill_(float(b.index))
+        class_order = []
+        for b in blocks:
+            ck = (b.rows, b.cols, eng._code(b))
+            if ck not in class_order:
+                class_order.append(ck)
+        for ck in class_order:
+            eng._after_class(ck)
+        eng._finish_collectives()
+        ok = all(bool((b.tensor == float(b.index)).all()) for b in blocks)
+        stats = eng.gather_stats({b.index: {"update_rms": 0.1 * b.index, "ratio": 0.01 * b.index}
+                                  for b in blocks if owner[b.index] == rank})
+        stats_ok = sorted(stats) == list(range(len(blocks))) and all(
+            abs(stats[i]["update_rms"] - 0.1 * i) < 1e-12 for i in stats)
+
+        # loss averaging of estimate_projection over the group
+        import muzo_clip_b200.muzo_optimizer as mo
+
+        class FakeEngine:
+            def __init__(self, opt, *a, **k):
+                self.device = torch.device("cpu")
+
+            def matches(self, opt):
+                return True
+
+            def perturb(self, seed, alpha):
+                pass
+
+        mo.StepEngine = FakeEngine
+        mo.MuZOClipOptimizer._engine_for_step = lambda self: self._engine or setattr(self, "_engine", FakeEngine(self)) or self._engine
+        model = torch.nn.Module()
+        model.q_proj = torch.nn.Linear(8, 8, bias=False)
+        opt = mo.MuZOClipOptimizer(model, seed=3, process_group=dist.group.WORLD)
+        losses = iter([1.0 + rank, 1.5 + 2 * rank])
+        proj = opt.estimate_projection(lambda: next(losses))
+        t = torch.tensor([proj["p_raw"], proj["seed"] % 1000003], dtype=torch.float64)
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        same_p = all(torch.equal(g, gathered[0]) for g in gathered)
+        Path(out_dir, f"rank{rank}.txt").write_text(f"{int(ok)} {int(stats_ok)} {int(same_p)} {owner}\n")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_collectives_on_two_gloo_ranks(tmp_path):
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    lines = [Path(tmp_path, f"rank{r}.txt").read_text().split(" ", 3) for r in range(world)]
+    for ok, stats_ok, same_p, owner in lines:
+        assert ok == "1" and stats_ok == "1" and same_p == "1"
+    assert lines[0][3] == lines[1][3]  # identical ownership on both ranks
+
+
+def test_collective_order_is_global_for_any_ownership():
+    """Each rank calls the class collectives in the global class order even when it owns no
+    block of some classes (the loop of StepEngine.run_step)."""
+    sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
+    from muzo_clip_b200._engine import StepEngine
+
+    src = Path(StepEngine.run_step.__code__.co_filename).read_text()
+    assert "while next_class < len(self.class_order)" in src

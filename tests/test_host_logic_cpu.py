@@ -1,0 +1,145 @@
+"""Host-side logic of MuZOClipOptimizer against the reference package, without a GPU.
+
+The device engine is replaced by a recording fake (test double); the reference runs on CPU
+tensors. With the same scripted losses both must produce identical seeds, projections, skip
+decisions, EMAs, learning-rate backoff, history and step guards (muzo_optimizer.py:190-371).
+"""
+
+from __future__ import annotations
+
+import math
+import sys
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+REF = "/root/reference"
+
+
+def _have_reference() -> bool:
+    from pathlib import Path
+
+    return (Path(REF) / "muzo_clip" / "__init__.py").exists()
+
+
+class FakeEngine:
+    def __init__(self, opt, *a, **k):
+        self.opt = opt
+        self.calls = []
+        self.blocks = [s for s in opt.selected_params]
+        self.device = torch.device("cpu")
+
+    def matches(self, opt):
+        return True
+
+    def perturb(self, seed, alpha):
+        self.calls.append(("perturb", seed, alpha))
+
+    def run_step(self, history, lr):
+        self.calls.append(("step", len(history), lr))
+        return {i: {"update_rms": 1e-6 * (i + 1), "ratio": 1e-3 * (i + 1)} for i in range(len(self.blocks))}
+
+
+def _model():
+    torch.manual_seed(0)
+    m = torch.nn.Module()
+    m.layers = torch.nn.ModuleList()
+    for _ in range(2):
+        blk = torch.nn.Module()
+        blk.q_proj = torch.nn.Linear(16, 16, bias=False)
+        blk.k_proj = torch.nn.Linear(16, 8, bias=False)
+        blk.norm = torch.nn.LayerNorm(16)
+        m.layers.append(blk)
+    m.lm_head = torch.nn.Linear(16, 4, bias=False)
+    return m
+
+
+LOSSES = [(2.0, 2.1), (2.05, 1.95), (float("nan"), 2.0), (2.0, 2.02), (9.0, 2.0), (1.99, 2.01), (2.0, 2.0),
+          (1.9, 2.0), (2.1, 1.9), (float("inf"), 1.0), (2.0, 1.98), (1.97, 2.0), (2.0, 2.03), (2.01, 2.0)]
+
+
+def _closure(seq):
+    it = iter(x for pair in seq for x in pair)
+    return lambda: next(it)
+
+
+@pytest.mark.skipif(not _have_reference(), reason="reference package not mounted")
+def test_projection_and_step_logic_match_reference(monkeypatch):
+    sys.path.insert(0, REF)
+    from muzo_clip import MuZOClipOptimizer as RefOpt
+
+    import muzo_clip_b200.muzo_optimizer as mo
+
+    monkeypatch.setattr(mo, "StepEngine", FakeEngine)
+    kw = dict(lr=1e-3, seed=77, horizon=6, min_history=3, loss_spike_ratio=2.0)
+    ref = RefOpt(_model(), **kw)
+    mine = mo.MuZOClipOptimizer(_model(), **kw)
+    assert mine.selected_parameter_names() == ref.selected_parameter_names()
+    c_ref, c_mine = _closure(LOSSES), _closure(LOSSES)
+    for _ in LOSSES:
+        a = ref.estimate_projection(c_ref)
+        b = mine.estimate_projection(c_mine)
+        for key in a:
+            va, vb = a[key], b[key]
+            if isinstance(va, float) and math.isnan(va):
+                assert math.isnan(vb)
+            else:
+                assert va == vb, (key, va, vb)
+        sa = ref.step()
+        sb = mine.step()
+        assert sa["skipped"] == sb["skipped"] and sa["skip_reason"] == sb["skip_reason"]
+        assert sa["lr"] == sb["lr"]
+        if not sa["skipped"]:
+            assert sa["updated_param_count"] == sb["updated_param_count"]
+        for attr in ("p_abs_ema", "loss_ema", "bad_step_count", "lr_scale", "_has_pending_update",
+                     "_last_step_updated"):
+            assert getattr(ref, attr) == getattr(mine, attr), attr
+        assert [tuple(h.__dict__.values()) for h in ref.history] == [tuple(h.__dict__.values()) for h in mine.history]
+
+
+def test_failed_closure_restores_perturbation(monkeypatch):
+    import muzo_clip_b200.muzo_optimizer as mo
+
+    monkeypatch.setattr(mo, "StepEngine", FakeEngine)
+    opt = mo.MuZOClipOptimizer(_model(), seed=5)
+    calls = {"n": 0}
+
+    def closure():
+        calls["n"] += 1
+        if calls["n"] == 2:
+            raise RuntimeError("forward failed")
+        return 1.0
+
+    with pytest.raises(RuntimeError):
+        opt.estimate_projection(closure)
+    ev = opt._engine.calls
+    # +eps, then -2eps, the failure at displacement -1 restores with +eps (muzo_optimizer.py:499-502)
+    assert [c[2] for c in ev] == [pytest.approx(1e-3), pytest.approx(-2e-3), pytest.approx(1e-3)]
+    assert len({c[1] for c in ev}) == 1
+    assert not opt.history
+
+
+def test_validation_errors_match_reference_messages():
+    import muzo_clip_b200.muzo_optimizer as mo
+
+    cases = [dict(horizon=0), dict(min_history=0), dict(min_history=9, horizon=8), dict(zo_eps=0.0),
+             dict(update_ratio_clip=0.0), dict(muon_scale=0.0), dict(distribution="uniform")]
+    msgs = ["horizon must be positive", "min_history must be positive",
+            "min_history must be less than or equal to horizon", "zo_eps must be positive",
+            "update_ratio_clip must be positive", "muon_scale must be positive", "Unsupported distribution: uniform"]
+    for kw, msg in zip(cases, msgs):
+        with pytest.raises(ValueError, match=msg):
+            mo.MuZOClipOptimizer(_model(), **kw)
+
+
+def test_cpu_tensors_are_rejected_not_computed():
+    from muzo_clip_b200 import make_zo_noise_like, zeropower_via_newtonschulz5
+
+    with pytest.raises(ValueError):
+        make_zo_noise_like(torch.zeros(4, 4), 1, "w")
+    with pytest.raises(ValueError):
+        zeropower_via_newtonschulz5(torch.ones(4, 4))
+    with pytest.raises(TypeError):
+        make_zo_noise_like(torch.zeros(4, 4, dtype=torch.int32), 1, "w")

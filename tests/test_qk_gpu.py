@@ -1,0 +1,166 @@
+"""QK-Clip on the GPU against the reference's eager-attention capture (qk_clip.py:161-322)."""
+
+from __future__ import annotations
+
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+import torch_reference as tr
+
+pytestmark = pytest.mark.gpu
+
+
+def _ulp(x: torch.Tensor, bits: int) -> torch.Tensor:
+    ax = x.abs().clamp_min(2.0 ** -126)
+    return torch.pow(2.0, torch.floor(torch.log2(ax)) - bits)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("b,hq,hkv,sq,sk,d", [(2, 8, 2, 100, 100, 64), (1, 4, 4, 64, 64, 128), (2, 6, 1, 33, 70, 32)])
+def test_qk_max_matches_eager_logits(device, dtype, causal, b, hq, hkv, sq, sk, d):
+    from muzo_clip_b200 import _qk
+
+    g = torch.Generator(device="cpu").manual_seed(b * 100 + hq + sq)
+    # HF layout: [B, S, H, D] viewed as [B, H, S, D] (non-contiguous, D contiguous)
+    q = (torch.randn((b, sq, hq, d), generator=g) * 2).to(dtype).to(device).transpose(1, 2)
+    k = (torch.randn((b, sk, hkv, d), generator=g) * 2).to(dtype).to(device).transpose(1, 2)
+    scale = d ** -0.5
+    ref = tr.qk_head_max(tr.eager_logits(q, k, scale, causal and sq <= sk))
+    got, valid = _qk.qk_head_max(q, k, scale, causal and sq <= sk, None)
+    torch.cuda.synchronize()
+    assert int(valid.item()) == 1
+    got = got.cpu()
+    bits = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 21}[dtype]
+    assert bool(((got - ref).abs() <= _ulp(ref, bits)).all()), (got, ref)
+
+
+def test_qk_max_flags_nonfinite(device):
+    from muzo_clip_b200 import _qk
+
+    q = torch.randn((1, 2, 16, 32), device=device, dtype=torch.bfloat16)
+    k = torch.randn((1, 2, 16, 32), device=device, dtype=torch.bfloat16)
+    q[0, 1, 3, 5] = float("inf")
+    _, valid = _qk.qk_head_max(q, k, 0.2, True, None)
+    assert int(valid.item()) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_logits_head_max_and_guarded_merge(device, dtype):
+    from muzo_clip_b200 import _qk
+
+    logits = (torch.randn((2, 5, 17, 23), device=device) * 4).to(dtype)
+    got, valid = _qk.logits_head_max(logits)
+    assert torch.equal(got.cpu(), tr.qk_head_max(logits)) and int(valid.item()) == 1
+    running = torch.full((5,), -1.0e9, device=device)
+    _qk.merge_max(running, got, valid)
+    assert torch.equal(running.cpu(), got.cpu())
+    bad = logits.clone()
+    bad[1, 2, 3, 4] = float("nan")
+    g2, v2 = _qk.logits_head_max(bad)
+    before = running.clone()
+    _qk.merge_max(running, g2 + 100.0, v2)  # dropped: the capture had a non-finite logit
+    assert int(v2.item()) == 0 and torch.equal(running, before)
+
+
+def _tiny_llama(dtype, device, kv_heads=2):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=kv_heads,
+                      intermediate_size=688, vocab_size=1024, attn_implementation="sdpa", initializer_range=0.02)
+    return LlamaForCausalLM(cfg).to(dtype=dtype, device=device).eval()
+
+
+def _reference_capture(model, ids):
+    """The reference's capture (qk_clip.py:91-118, 173-196) restated: eager attention, softmax
+    input of each attention module reduced to per-head maxima."""
+    import torch.nn.functional as F
+
+    names = {id(m): n for n, m in model.named_modules() if hasattr(m, "q_proj") and hasattr(m, "k_proj")}
+    stack, captured = [], {}
+    hooks = []
+    for mod_id, name in names.items():
+        mod = next(m for m in model.modules() if id(m) == mod_id)
+        hooks.append(mod.register_forward_pre_hook(lambda m, a, name=name: stack.append(name)))
+        hooks.append(mod.register_forward_hook(lambda m, a, o: stack.pop()))
+    orig = F.softmax
+
+    def patched(inp, *args, **kwargs):
+        if stack and inp.ndim == 4:
+            per = inp.detach().float().amax(dim=(0, 2, 3)).cpu()
+            prev = captured.get(stack[-1])
+            captured[stack[-1]] = per if prev is None else torch.maximum(prev, per)
+        return orig(inp, *args, **kwargs)
+
+    saved = model.config._attn_implementation
+    model.config._attn_implementation = "eager"
+    F.softmax = patched
+    try:
+        with torch.no_grad():
+            model(input_ids=ids)
+    finally:
+        F.softmax = orig
+        model.config._attn_implementation = saved
+        for h in hooks:
+            h.remove()
+    return captured
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_probe_and_apply_matches_reference(device, dtype):
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = _tiny_llama(dtype, device)
+    # make some heads exceed tau so clipping happens
+    with torch.no_grad():
+        model.model.layers[0].self_attn.q_proj.weight.mul_(40.0)
+        model.model.layers[1].self_attn.k_proj.weight[:64].mul_(30.0)
+    twin = copy.deepcopy(model)
+    ids = torch.randint(0, 1024, (4, 64), generator=torch.Generator().manual_seed(1)).to(device)
+    ref_smax = _reference_capture(twin, ids)
+    tau, alpha = 20.0, 0.5
+    opt = MuZOClipOptimizer(model, enable_qk_clip=True, qk_clip_tau=tau, qk_clip_alpha=alpha)
+    # capture only, to compare the maxima before any scaling
+    ctrl = opt.qk_clip
+    ctrl.clear()
+    with ctrl.force_eager_attention(True):
+        with ctrl.capture():
+            with torch.no_grad():
+                model(input_ids=ids)
+    bits = 7 if dtype == torch.bfloat16 else 21
+    assert set(ctrl._captured_smax) == set(ref_smax)
+    for name, ref in ref_smax.items():
+        got = ctrl._captured_smax[name].cpu()
+        assert bool(((got - ref).abs() <= _ulp(ref, bits)).all()), (name, got, ref)
+    stats = ctrl.apply()
+    # the reference's scaling on the twin with the reference maxima
+    count = 0
+    smax_max = 0.0
+    for name, smax in ref_smax.items():
+        mod = twin.get_submodule(name)
+        smax_max = max(smax_max, float(smax.max()))
+        c, _ = tr.qk_scale(mod.q_proj.weight.data, mod.k_proj.weight.data, smax, tau, alpha)
+        count += c
+    assert stats.enabled and stats.exact_logits and not stats.fallback_used
+    assert stats.qk_clip_count == count and count > 0
+    assert abs(stats.qk_smax_max - smax_max) <= 2.0 ** -bits * smax_max
+    for (n1, p1), (_, p2) in zip(model.named_parameters(), twin.named_parameters()):
+        if "q_proj" in n1 or "k_proj" in n1:
+            diff = (p1.float() - p2.float()).abs()
+            assert bool((diff <= _ulp(p2.float(), bits)).all()), n1
+            assert (p1 == p2).float().mean().item() > 0.99
+        else:
+            assert torch.equal(p1, p2), n1
+
+
+def test_probe_reports_disabled_without_modules(device):
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = torch.nn.Sequential(torch.nn.Linear(8, 8)).to(device)
+    opt = MuZOClipOptimizer(model, enable_qk_clip=True)
+    st = opt.probe_and_apply_qk_clip(lambda: torch.tensor(1.0))
+    assert st["enabled"] is False and st["disabled_reason"] == "no q_proj/k_proj attention modules found"
