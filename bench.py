@@ -242,11 +242,14 @@ def run_gpu(args) -> int:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # timed region: device time by CUDA events, wall time through the public API
+    # timed region: device time by CUDA events on the launching stream (per phase as well),
+    # wall time through the public API
+    engine = opt._engine
     barrier()
     launches0 = _lib.launch_count
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    engine.start_phase_timing()
     with ClockSampler(local) as clocks:
         w0 = time.perf_counter()
         start.record(stream)
@@ -255,6 +258,7 @@ def run_gpu(args) -> int:
         end.record(stream)
         barrier()
         w1 = time.perf_counter()
+    phases = {k: v / args.steps for k, v in engine.stop_phase_timing().items()}
     launches = _lib.launch_count - launches0
     dev_ms = start.elapsed_time(end) / args.steps
     wall_ms = (w1 - w0) * 1e3 / args.steps
@@ -263,26 +267,28 @@ def run_gpu(args) -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms, wall_ms = t.tolist()
 
-    # phase breakdown (untimed, after the timed region): one perturb pass and one step with
-    # per-phase events
-    engine = opt._engine
-    perturb_ms = []
-    for _ in range(3):
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        engine.perturb(4242, 1e-3)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        perturb_ms.append(e0.elapsed_time(e1))
-        engine.perturb(4242, -1e-3)
-    perturb_ms = statistics.median(perturb_ms)
+    perturb_ms = phases.get("perturb", 0.0) / 3.0          # three passes per step
     perturb_bytes = 4.0 * total_numel(args.layers)
-    perturb_gbs = perturb_bytes / (perturb_ms * 1e-3) / 1e9
-    phases = engine.profile_step(opt.history, opt.current_lr)
+    perturb_gbs = perturb_bytes / (perturb_ms * 1e-3) / 1e9 if perturb_ms > 0 else 0.0
     ns_ms = phases.get("ns", 0.0)
     ns_flops = engine.owned_ns_flops()
+    ns_exec = engine.owned_ns_flops_executed()
     ns_tflops = ns_flops / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+    ns_exec_tflops = ns_exec / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+
+    # Rademacher perturbation bandwidth (untimed, after the timed region): one pass over the
+    # same matrices through an optimizer configured for Rademacher noise
+    rad = MuZOClipOptimizer(model, distribution="rademacher", seed=4321)
+    rad_engine = rad._engine_for_step()
+    for _ in range(3):
+        rad_engine.perturb(777, 1e-3)
+    torch.cuda.synchronize()
+    rad_engine.start_phase_timing()
+    for _ in range(4):
+        rad_engine.perturb(777, 1e-3)
+        rad_engine.perturb(777, -1e-3)
+    rad_ms = rad_engine.stop_phase_timing().get("perturb", 0.0) / 8.0
+    rad_gbs = perturb_bytes / (rad_ms * 1e-3) / 1e9 if rad_ms > 0 else 0.0
 
     if rank == 0:
         peaks = load_peaks()
@@ -309,21 +315,27 @@ def run_gpu(args) -> int:
                        "l2": "inputs larger than L2 (14 GB of weights per pass)"},
             "perturb_gbs": round(perturb_gbs, 1),
             "perturb_ms": round(perturb_ms, 3),
+            "perturb_gbs_rademacher": round(rad_gbs, 1),
             "phase_ms": {k: round(v, 3) for k, v in phases.items()},
+            "other_ms": round(dev_ms - sum(phases.values()), 3),
             "ns_tflops": round(ns_tflops, 1),
             "roofline": {
                 "bound": "tensor",
-                "kernel": "ns_gemm_kernel (Newton-Schulz GEMMs, all launches of one step)",
+                "kernel": "ns_gemm_kernel (Newton-Schulz GEMMs; all launches of the timed steps)",
                 "achieved": round(ns_tflops, 1),
                 "peak": peaks["bf16_tflops_sustained"],
                 "unit": "TFLOP/s",
                 "frac": round(ns_tflops / peaks["bf16_tflops_sustained"], 4),
+                "flops": "dense 5*(4m^2n+2m^3) per matrix; symmetric tiles execute fewer",
+                "executed_tflops": round(ns_exec_tflops, 1),
+                "executed_frac": round(ns_exec_tflops / peaks["bf16_tflops_sustained"], 4),
                 "peak_source": f"{peaks['source']} bf16 sustained",
                 "traffic": None,
             },
             "perturb_roofline": {
                 "bound": "hbm", "achieved": round(perturb_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(perturb_gbs / peaks["hbm_gbs"], 4), "peak_source": f"{peaks['source']} copy",
+                "rademacher_achieved": round(rad_gbs, 1), "rademacher_frac": round(rad_gbs / peaks["hbm_gbs"], 4),
             },
             "e2e": {"value": round(wall_ms, 3), "unit": "ms/step", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},

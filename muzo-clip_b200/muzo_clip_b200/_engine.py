@@ -190,6 +190,7 @@ class StepEngine:
         keys = self.keys_for(seed)
         stream = _lib.stream_ptr(self.device)
         dev_keys = self.uploader.upload(keys)
+        self._mark("perturb", True)
         alpha32 = float(np.float32(alpha))
         for g in self.perturb_groups:
             idx = np.fromiter((b.index for b in g.blocks), dtype=np.int64, count=len(g.blocks))
@@ -197,8 +198,9 @@ class StepEngine:
                 kptr = dev_keys.data_ptr()
             else:
                 kptr = self.uploader.upload(keys[idx]).data_ptr()
-            _lib.launch("muzo_perturb_segments", g.table.data_ptr(), g.nsegs, g.total_items, kptr,
-                                               g.dtype_code, self.dist, alpha32, stream)
+            _lib.launch("muzo_perturb_segments", g.table.data_ptr(), g.nsegs, g.total_items, kptr, g.dtype_code,
+                        self.dist, alpha32, stream)
+        self._mark("perturb", False)
 
     # ------------------------------------------------------------------ step
     def _workspace_budget(self) -> int:
@@ -281,6 +283,26 @@ class StepEngine:
 
     def owned_ns_flops(self) -> float:
         return sum(ns_flops(b.rows, b.cols, self.opt.ns_steps) for b in self.owned)
+
+    def owned_ns_flops_executed(self) -> float:
+        """FLOPs the tensor cores execute: X X^T and b A + c A A only on the tiles that meet the
+        upper triangle (128 x 256 tiles), a X + B X in full."""
+        tot = 0.0
+        for b in self.owned:
+            m, n = min(b.rows, b.cols), max(b.rows, b.cols)
+            tm, tn = -(-m // 128), -(-m // 256)
+            frac = sum(tn - (r * 128) // 256 for r in range(tm)) / float(tm * tn)
+            tot += self.opt.ns_steps * (frac * (2.0 * m * m * n + 2.0 * m ** 3) + 2.0 * m * m * n)
+        return tot
+
+    def start_phase_timing(self) -> None:
+        self._phase_events = {}
+
+    def stop_phase_timing(self) -> dict[str, float]:
+        """Milliseconds per phase accumulated since start_phase_timing (synchronises)."""
+        ev_map, self._phase_events = self._phase_events or {}, None
+        torch.cuda.synchronize(self.device)
+        return {k: sum(a.elapsed_time(b) for a, b in v) for k, v in ev_map.items()}
 
     def profile_step(self, history, lr: float) -> dict[str, float]:
         """Run one step with CUDA events around each phase; returns milliseconds per phase

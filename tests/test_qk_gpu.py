@@ -86,7 +86,7 @@ def _reference_capture(model, ids):
     for mod_id, name in names.items():
         mod = next(m for m in model.modules() if id(m) == mod_id)
         hooks.append(mod.register_forward_pre_hook(lambda m, a, name=name: stack.append(name)))
-        hooks.append(mod.register_forward_hook(lambda m, a, o: stack.pop()))
+        hooks.append(mod.register_forward_hook(lambda m, a, o: stack.pop() and None))  # must return None
     orig = F.softmax
 
     def patched(inp, *args, **kwargs):
