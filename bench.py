@@ -379,8 +379,111 @@ def run_reference(args) -> int:
     return 0
 
 
+# ---------------------------------------------------------------- single-kernel cases
+# Small, self-contained workloads of one kernel family, used for ncu captures and for the
+# Newton-Schulz (batch of 8 per shape) and bandwidth (1 M - 2 G elements, horizon 1-16) sweeps.
+
+
+def _event_ms(fn, reps: int, stream) -> float:
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def run_case(args) -> int:
+    from muzo_clip_b200 import _lib
+    from muzo_clip_b200._engine import ns_flops
+    from muzo_clip_b200.newton_schulz import allocate_ns_buffers, ns_iterations
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+    peaks = load_peaks()
+    out = {"case": args.case}
+    if args.case == "ns":
+        buf = allocate_ns_buffers(args.rows, args.cols, args.batch, device)
+        buf.x.normal_(0.0, 1.0 / math.sqrt(args.rows * args.cols))
+        status = torch.zeros(4, dtype=torch.int32, device=device)
+        run = lambda: ns_iterations(buf, args.batch, 5, 0, status.data_ptr(), sp, 0 if args.dense else 1)  # noqa: E731
+        for _ in range(args.warmup):
+            run()
+        ms = _event_ms(run, args.steps, stream)
+        fl = args.batch * ns_flops(args.rows, args.cols, 5)
+        out.update(rows=args.rows, cols=args.cols, batch=args.batch, symmetric=not args.dense, ms=round(ms, 3),
+                   dense_tflops=round(fl / ms / 1e9, 1), status=int(status[0]))
+    elif args.case in ("perturb", "rebuild"):
+        numel = args.numel
+        cols = 4096 if numel % 4096 == 0 else 1
+        w = torch.empty((numel // cols, cols), dtype=torch.bfloat16, device=device)
+        w.normal_(0.0, 0.02)
+        dist_code = _lib.dist_code(args.dist)
+        sms, thr = _lib.device_geometry(device)
+        keys = torch.tensor(np.arange(1, args.horizon + 1, dtype=np.int64) * 7919, device=device)
+        if args.case == "perturb":
+            segs, total = _lib.plan_segments([numel], [w.data_ptr()], None, dist_code, sms, thr)
+            table = _lib.to_device_table(segs, device)
+            run = lambda: _lib.launch("muzo_perturb_segments", table.data_ptr(), len(segs), total,  # noqa: E731
+                                      keys.data_ptr(), _lib.BF16, dist_code, 1e-3, sp)
+            nbytes = 4.0 * numel
+        else:
+            x = torch.empty_like(w)
+            segs, total = _lib.plan_segments([numel], [w.data_ptr()], [x.data_ptr()], dist_code, sms, thr)
+            table = _lib.to_device_table(segs, device)
+            alphas = torch.full((args.horizon,), 0.1, dtype=torch.float32, device=device)
+            sums = torch.zeros(_lib.NSUMS, dtype=torch.float64, device=device)
+            flags = torch.zeros(4, dtype=torch.int32, device=device)
+            run = lambda: _lib.launch("muzo_rebuild_segments", table.data_ptr(), len(segs), total,  # noqa: E731
+                                      keys.data_ptr(), alphas.data_ptr(), args.horizon, dist_code, _lib.BF16, 1, 0.5,
+                                      sums.data_ptr(), flags.data_ptr(), 0, sp)
+            nbytes = 4.0 * numel  # bf16(M) write + W read
+        for _ in range(args.warmup):
+            run()
+        ms = _event_ms(run, args.steps, stream)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out.update(numel=numel, dist=args.dist, horizon=args.horizon if args.case == "rebuild" else None,
+                   ms=round(ms, 4), gbs=round(gbs, 1), hbm_frac=round(gbs / peaks["hbm_gbs"], 4))
+    elif args.case == "qk":
+        # per-head max logit of one attention layer: Q [B, Hq, S, D], K [B, Hkv, S, D] as the
+        # transposed views of [B, S, H, D] that transformers passes to attention functions
+        from muzo_clip_b200 import _qk
+
+        b, hq, hkv, seq, d = args.batch, args.heads, args.kv_heads, args.seq, args.head_dim
+        q = torch.randn((b, seq, hq, d), device=device, dtype=torch.bfloat16).transpose(1, 2)
+        k = torch.randn((b, seq, hkv, d), device=device, dtype=torch.bfloat16).transpose(1, 2)
+        run = lambda: _qk.qk_head_max(q, k, d ** -0.5, True, None)  # noqa: E731
+        for _ in range(args.warmup):
+            run()
+        ms = _event_ms(run, args.steps, stream)
+        flops = 2.0 * b * hq * seq * seq * d / 2.0  # causal half
+        out.update(batch=b, heads=hq, kv_heads=hkv, seq=seq, head_dim=d, ms_per_layer=round(ms, 4),
+                   causal_tflops=round(flops / ms / 1e9, 1))
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, choices=["ns", "perturb", "rebuild", "qk"],
+                    help="run one kernel family on a small workload instead of the optimizer step")
+    ap.add_argument("--rows", type=int, default=4096)
+    ap.add_argument("--cols", type=int, default=4096)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--dense", action="store_true", help="ns case: compute every output tile")
+    ap.add_argument("--numel", type=int, default=1 << 28)
+    ap.add_argument("--dist", default="rademacher", choices=["normal", "rademacher"])
+    ap.add_argument("--horizon", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--heads", type=int, default=64)
+    ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--head-dim", type=int, default=128)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -388,6 +491,8 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.case is not None:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)

@@ -16,52 +16,52 @@
 namespace muzo {
 namespace {
 
+// Philox4x32 with 10 rounds (Salmon, Moraes, Dror, Shaw, "Parallel Random Numbers: As Easy as
+// 1, 2, 3", SC'11): per round two 32x32->64 multiplies of counter words 0 and 2 by the published
+// multipliers, a swap-and-xor with the round key, and a Weyl increment of the key.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
+    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// The four 32-bit words torch's generator gives launch thread t on loop trip `trip`: the Philox
+// block whose counter holds (trip + offset/4) in its low 64 bits and t in its high 64 bits.
+__device__ __forceinline__ uint4 thread_words(uint64_t key, uint64_t t, uint64_t word_offset, uint64_t trip) {
+  const uint64_t blk = trip + (word_offset >> 2);
+  return philox4x32_10(make_uint4(static_cast<uint32_t>(blk), static_cast<uint32_t>(blk >> 32),
+                                  static_cast<uint32_t>(t), static_cast<uint32_t>(t >> 32)),
+                       static_cast<uint32_t>(key), static_cast<uint32_t>(key >> 32));
+}
+
 // Noise of 8 consecutive launch threads t0..t0+7 for loop trip `trip`: z[j][k] is element
-// t0 + k + S*(4*trip + j). `word_offset` is the launch's Philox offset (32-bit words).
+// t0 + k + S*(4*trip + j). `word_offset` is the launch's Philox offset (32-bit words). Normal
+// noise calls cuRAND's Box-Muller transform on the same Philox stream (curand_normal4).
 template <int DIST>
 __device__ __forceinline__ void noise8x4(uint64_t key, uint64_t t0, uint64_t word_offset,
                                          uint64_t trip, float (&z)[4][8]) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    curandStatePhilox4_32_10_t st;
-    curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
     if (DIST == MUZO_NORMAL) {
+      curandStatePhilox4_32_10_t st;
+      curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
       float4 n = curand_normal4(&st);
       // randn's transform is rand * std + mean with std = 1, mean = 0
       z[0][k] = n.x; z[1][k] = n.y; z[2][k] = n.z; z[3][k] = n.w;
     } else {
-      uint4 r = curand4(&st);
+      const uint4 r = thread_words(key, t0 + k, word_offset, trip);
       // randint(0, 2) keeps word % 2; the reference maps it to 2*b - 1
       z[0][k] = (r.x & 1u) ? 1.0f : -1.0f;
       z[1][k] = (r.y & 1u) ? 1.0f : -1.0f;
       z[2][k] = (r.z & 1u) ? 1.0f : -1.0f;
       z[3][k] = (r.w & 1u) ? 1.0f : -1.0f;
     }
-  }
-}
-
-// acc[j][k] += alpha * float(dtype(z[j][k])) for the noise of threads t0..t0+7 (trip `trip`),
-// one thread's Philox block at a time so only four noise values are live.
-template <int DIST, int PDTYPE>
-__device__ __forceinline__ void accumulate8x4(uint64_t key, uint64_t t0, uint64_t word_offset, uint64_t trip,
-                                              float alpha, float (&acc)[4][8]) {
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    curandStatePhilox4_32_10_t st;
-    curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
-    float z[4];
-    if (DIST == MUZO_NORMAL) {
-      float4 n = curand_normal4(&st);
-      z[0] = n.x; z[1] = n.y; z[2] = n.z; z[3] = n.w;
-    } else {
-      uint4 r = curand4(&st);
-      z[0] = (r.x & 1u) ? 1.0f : -1.0f;
-      z[1] = (r.y & 1u) ? 1.0f : -1.0f;
-      z[2] = (r.z & 1u) ? 1.0f : -1.0f;
-      z[3] = (r.w & 1u) ? 1.0f : -1.0f;
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j][k] = __fmaf_rn(alpha, round_to(z[j], PDTYPE), acc[j][k]);
   }
 }
 
@@ -134,9 +134,37 @@ fill_noise_kernel(const muzo_segment* __restrict__ segs, int nsegs, uint64_t key
 // --------------------------------------------------------------------------- perturb
 
 // W <- dtype(W + alpha * dtype(Z)). torch's add_(noise, alpha) evaluates a + alpha * b in fp32,
-// which nvcc contracts to one fused multiply-add.
+// which nvcc contracts to one fused multiply-add; for Rademacher noise (z = +-1, exact) that is
+// w +- alpha. The weights of an item are loaded (still packed) before the Philox work so their
+// latency overlaps it; Rademacher noise is kept as one sign bit per element.
+template <int DTYPE>
+struct Packed8 {
+  uint4 a, b;  // 8 elements: 16 bytes for 16-bit types, 32 bytes for fp32
+  __device__ __forceinline__ void load(const void* base, int64_t i) {
+    if (DTYPE == MUZO_F32) {
+      const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(base) + i);
+      a = p[0]; b = p[1];
+    } else {
+      a = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + i);
+    }
+  }
+  __device__ __forceinline__ void unpack(float (&v)[8]) const {
+    if (DTYPE == MUZO_F32) {
+      v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+      v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y); v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
+    } else {
+      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (DTYPE == MUZO_BF16) { v[2 * q] = bf16_lo(w[q]); v[2 * q + 1] = bf16_hi(w[q]); }
+        else { v[2 * q] = half_lo(w[q]); v[2 * q + 1] = half_hi(w[q]); }
+      }
+    }
+  }
+};
+
 template <int DIST, int DTYPE>
-__global__ void __launch_bounds__(kElemThreads)
+__global__ void __launch_bounds__(kElemThreads, 4)
 perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
                float alpha) {
   const SegView sv = cta_segment(segs, nsegs, DTYPE, DTYPE);
@@ -150,22 +178,60 @@ perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
     const uint32_t oct = local - trip * octets;
     const int64_t li0 = static_cast<int64_t>(sv.threads) * (4ll * trip) + 8ll * oct;
     if (li0 >= sv.numel) continue;
-    float z[4][8];
-    noise8x4<DIST>(key, 8ull * oct, sv.philox_offset, trip, z);
+    if constexpr (DIST == MUZO_RADEMACHER) {
+      // memory-bound: the packed weight loads go out before the Philox work (16-bit types)
+      constexpr bool kHoist = DTYPE != MUZO_F32;
+      Packed8<DTYPE> raw[4];
+      if (kHoist) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
-      if (li >= sv.numel) break;
-      if (vec && li + 8 <= sv.numel) {
+        for (int j = 0; j < 4; ++j) {
+          const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
+          if (vec && li + 8 <= sv.numel) raw[j].load(sv.param, li);
+        }
+      }
+      uint32_t sbits[4] = {0u, 0u, 0u, 0u};  // one sign bit per element
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint4 r = thread_words(key, 8ull * oct + k, sv.philox_offset, trip);
+        sbits[0] |= (r.x & 1u) << k; sbits[1] |= (r.y & 1u) << k;
+        sbits[2] |= (r.z & 1u) << k; sbits[3] |= (r.w & 1u) << k;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
+        if (li >= sv.numel) break;
+        const int cnt = li + 8 <= sv.numel ? 8 : static_cast<int>(sv.numel - li);
         float w[8];
-        load8(sv.param, li, DTYPE, w);
+        if (vec && cnt == 8) {
+          if (!kHoist) raw[j].load(sv.param, li);
+          raw[j].unpack(w);
+        } else {
+          for (int k = 0; k < 8; ++k) w[k] = k < cnt ? load_elem(sv.param, li + k, DTYPE) : 0.0f;
+        }
 #pragma unroll
-        for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w[k]);
-        store8(sv.param, li, DTYPE, w);
-      } else {
-        for (int k = 0; k < 8 && li + k < sv.numel; ++k) {
-          float w = load_elem(sv.param, li + k, DTYPE);
-          store_elem(sv.param, li + k, DTYPE, __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w));
+        for (int k = 0; k < 8; ++k) w[k] = __fadd_rn(w[k], ((sbits[j] >> k) & 1u) ? alpha : -alpha);
+        if (vec && cnt == 8) store8(sv.param, li, DTYPE, w);
+        else for (int k = 0; k < cnt; ++k) store_elem(sv.param, li + k, DTYPE, w[k]);
+      }
+    } else {
+      // normal noise: bound by the Box-Muller arithmetic; weights loaded after it
+      float z[4][8];
+      noise8x4<DIST>(key, 8ull * oct, sv.philox_offset, trip, z);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
+        if (li >= sv.numel) break;
+        if (vec && li + 8 <= sv.numel) {
+          float w[8];
+          load8(sv.param, li, DTYPE, w);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w[k]);
+          store8(sv.param, li, DTYPE, w);
+        } else {
+          for (int k = 0; k < 8 && li + k < sv.numel; ++k) {
+            const float w = load_elem(sv.param, li + k, DTYPE);
+            store_elem(sv.param, li + k, DTYPE, __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w));
+          }
         }
       }
     }
@@ -174,18 +240,23 @@ perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
 
 // --------------------------------------------------------------------------- rebuild
 
-// Block-wide fp64 reduction of three partial sums followed by one atomicAdd per sum.
-__device__ __forceinline__ void block_accumulate3(double a, double b, double c, double* dst_a,
-                                                  double* dst_b, double* dst_c) {
-  __shared__ double red[3][kElemThreads / 32];
+// The rebuild runs 512-thread CTAs in which two threads share a work item: each takes four of
+// its eight launch threads (a quad), so a thread holds 16 accumulators instead of 32 and an SM
+// keeps twice as many warps in flight to hide the Philox / Box-Muller latency.
+constexpr int kRebuildThreads = 2 * kElemThreads;
+
+template <int N>
+__device__ __forceinline__ void block_accumulate3(double a, double b, double c, double* dst_a, double* dst_b,
+                                                  double* dst_c) {
+  __shared__ double red[3][N / 32];
   a = warp_sum(a); b = warp_sum(b); c = warp_sum(c);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) { red[0][warp] = a; red[1][warp] = b; red[2][warp] = c; }
   __syncthreads();
   if (warp == 0) {
-    a = lane < kElemThreads / 32 ? red[0][lane] : 0.0;
-    b = lane < kElemThreads / 32 ? red[1][lane] : 0.0;
-    c = lane < kElemThreads / 32 ? red[2][lane] : 0.0;
+    a = lane < N / 32 ? red[0][lane] : 0.0;
+    b = lane < N / 32 ? red[1][lane] : 0.0;
+    c = lane < N / 32 ? red[2][lane] : 0.0;
     a = warp_sum(a); b = warp_sum(b); c = warp_sum(c);
     if (lane == 0) {
       if (a != 0.0) atomicAdd(dst_a, a);
@@ -193,6 +264,53 @@ __device__ __forceinline__ void block_accumulate3(double a, double b, double c, 
       if (c != 0.0) atomicAdd(dst_c, c);
     }
   }
+  __syncthreads();  // red is reused by the next chunk
+}
+
+// acc[j][k] += alpha * float(dtype(z)) for launch threads t0..t0+3 of loop trip `trip`.
+template <int DIST, int PDTYPE>
+__device__ __forceinline__ void accumulate4x4(uint64_t key, uint64_t t0, uint64_t word_offset, uint64_t trip,
+                                              float alpha, float (&acc)[4][4]) {
+  // normal noise: one Box-Muller block at a time (its temporaries are large; warps, not
+  // unrolling, hide the latency); Rademacher: fully unrolled
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (DIST == MUZO_NORMAL && k > 0) asm volatile("" ::: "memory");
+    if (DIST == MUZO_NORMAL) {
+      curandStatePhilox4_32_10_t st;
+      curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
+      const float4 n = curand_normal4(&st);
+      acc[0][k] = __fmaf_rn(alpha, round_to(n.x, PDTYPE), acc[0][k]);
+      acc[1][k] = __fmaf_rn(alpha, round_to(n.y, PDTYPE), acc[1][k]);
+      acc[2][k] = __fmaf_rn(alpha, round_to(n.z, PDTYPE), acc[2][k]);
+      acc[3][k] = __fmaf_rn(alpha, round_to(n.w, PDTYPE), acc[3][k]);
+    } else {
+      // z = +-1 is exact in every dtype and alpha * z is exact: acc + alpha*z == acc +- alpha
+      const uint4 r = thread_words(key, t0 + k, word_offset, trip);
+      acc[0][k] = __fadd_rn(acc[0][k], (r.x & 1u) ? alpha : -alpha);
+      acc[1][k] = __fadd_rn(acc[1][k], (r.y & 1u) ? alpha : -alpha);
+      acc[2][k] = __fadd_rn(acc[2][k], (r.z & 1u) ? alpha : -alpha);
+      acc[3][k] = __fadd_rn(acc[3][k], (r.w & 1u) ? alpha : -alpha);
+    }
+  }
+}
+
+__device__ __forceinline__ void load4(const void* base, int64_t i, int dtype, float (&v)[4]) {
+  if (dtype == MUZO_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(base) + i);
+    if (dtype == MUZO_BF16) { v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y); }
+    else { v[0] = half_lo(u.x); v[1] = half_hi(u.x); v[2] = half_lo(u.y); v[3] = half_hi(u.y); }
+  }
+}
+
+__device__ __forceinline__ void store4_bf16(void* base, int64_t i, const float (&v)[4]) {
+  uint2 u;
+  u.x = pack_bf16(v[0], v[1]);
+  u.y = pack_bf16(v[2], v[3]);
+  *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(base) + i) = u;
 }
 
 // M = sum_h alphas[h] * float(dtype(Z_h)) (h = age, newest first, as the reference walks
@@ -207,41 +325,43 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
   const uint32_t octets = sv.threads / 8;
   const bool vec = vec_ok(sv.out, 0, MUZO_BF16) && vec_ok(sv.param, 0, PDTYPE);
   const uint64_t* bkeys = keys + static_cast<int64_t>(sv.block) * horizon;
+  const int half = threadIdx.x & 1;          // which quad of the item's eight launch threads
+  const int slot = threadIdx.x >> 1;         // item slot within the CTA's 256-item stride
   double m2 = 0.0, x2 = 0.0, w2 = 0.0;
   bool finite = true;
 #pragma unroll 1
   for (int it = 0; it < kItemsPerThread; ++it) {
-    const uint32_t local = static_cast<uint32_t>(sv.local_item0) + it * kElemThreads + threadIdx.x;
+    const uint32_t local = static_cast<uint32_t>(sv.local_item0) + it * kElemThreads + slot;
     const uint32_t trip = local / octets;
     const uint32_t oct = local - trip * octets;
-    const int64_t li0 = static_cast<int64_t>(sv.threads) * (4ll * trip) + 8ll * oct;
+    const int64_t li0 = static_cast<int64_t>(sv.threads) * (4ll * trip) + 8ll * oct + 4 * half;
     if (li0 >= sv.numel) continue;
-    float acc[4][8];
+    float acc[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[j][k] = 0.0f;
+      for (int k = 0; k < 4; ++k) acc[j][k] = 0.0f;
 #pragma unroll 1
     for (int h = 0; h < horizon; ++h)
-      accumulate8x4<DIST, PDTYPE>(bkeys[h], 8ull * oct, sv.philox_offset, trip, alphas[h], acc);
+      accumulate4x4<DIST, PDTYPE>(bkeys[h], 8ull * oct + 4 * half, sv.philox_offset, trip, alphas[h], acc);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
       if (li >= sv.numel) break;
-      float m[8], w[8];
-      const int cnt = li + 8 <= sv.numel ? 8 : static_cast<int>(sv.numel - li);
+      float m[4], w[4];
+      const int cnt = li + 4 <= sv.numel ? 4 : static_cast<int>(sv.numel - li);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m[k] = normalize ? acc[j][k] * inv_coeff_sum : acc[j][k];
-      if (vec && cnt == 8) {
-        load8(sv.param, li, PDTYPE, w);
-        store8(sv.out, li, MUZO_BF16, m);
+      for (int k = 0; k < 4; ++k) m[k] = normalize ? acc[j][k] * inv_coeff_sum : acc[j][k];
+      if (vec && cnt == 4) {
+        load4(sv.param, li, PDTYPE, w);
+        store4_bf16(sv.out, li, m);
       } else {
-        for (int k = 0; k < 8; ++k) w[k] = k < cnt ? load_elem(sv.param, li + k, PDTYPE) : 0.0f;
+        for (int k = 0; k < 4; ++k) w[k] = k < cnt ? load_elem(sv.param, li + k, PDTYPE) : 0.0f;
         for (int k = 0; k < cnt; ++k) store_elem(sv.out, li + k, MUZO_BF16, m[k]);
       }
       float pm = 0.0f, px = 0.0f, pw = 0.0f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 4; ++k) {
         if (k < cnt) {
           finite = finite && isfinite(m[k]);
           const float xb = bf16r(m[k]);
@@ -254,12 +374,12 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
     }
   }
   double* bs = sums + static_cast<int64_t>(sv.block) * MUZO_NSUMS;
-  block_accumulate3(m2, x2, w2, bs + MUZO_SUM_M2, bs + MUZO_SUM_X2, bs + MUZO_SUM_W2);
+  block_accumulate3<kRebuildThreads>(m2, x2, w2, bs + MUZO_SUM_M2, bs + MUZO_SUM_X2, bs + MUZO_SUM_W2);
   if (!finite) atomicOr(flags + sv.block, MUZO_FLAG_NONFINITE_INPUT);
 }
 
 template <int DIST, int PDTYPE>
-__global__ void __launch_bounds__(kElemThreads, 2)
+__global__ void __launch_bounds__(kRebuildThreads, 2)
 rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
                const float* __restrict__ alphas, int horizon, int normalize, float inv_coeff_sum,
                double* __restrict__ sums, int32_t* __restrict__ flags, int64_t nchunks) {
@@ -348,10 +468,10 @@ int muzo_rebuild_segments(const muzo_segment* d_segs, int nsegs, int64_t total_i
   st = dispatch_dtype(param_dtype, [&](auto d) {
     constexpr int D = decltype(d)::value;
     if (dist == MUZO_NORMAL)
-      rebuild_kernel<MUZO_NORMAL, D><<<grid, kElemThreads, 0, s>>>(
+      rebuild_kernel<MUZO_NORMAL, D><<<grid, kRebuildThreads, 0, s>>>(
           d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags, nchunks);
     else
-      rebuild_kernel<MUZO_RADEMACHER, D><<<grid, kElemThreads, 0, s>>>(
+      rebuild_kernel<MUZO_RADEMACHER, D><<<grid, kRebuildThreads, 0, s>>>(
           d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags, nchunks);
   });
   if (st != MUZO_OK) return st;

@@ -8,10 +8,7 @@
 //               256-column TMEM accumulators, so the epilogue of tile i overlaps tile i+1;
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, apply the fused op, store bf16.
 // Every wait is bounded; on timeout the kernel records an error code, drains and returns.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include "muzo_common.cuh"
+#include "tcgen05_common.cuh"
 
 namespace muzo {
 namespace {
@@ -29,108 +26,7 @@ constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 2 * BN;       // two accumulators of BN fp32 columns
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
-constexpr unsigned long long kWaitLimitCycles = 4ull * 1000 * 1000 * 1000;  // ~2 s at 2 GHz
-
-enum : int { kErrNone = 0, kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutEpilogue = 3 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Bounded wait for the phase with parity `parity` to complete. Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
-  const long long start = clock64();
-  while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
-    if (static_cast<unsigned long long>(clock64() - start) > kWaitLimitCycles) return false;
-  }
-}
-
-__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0,
-                                            int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// 32 lanes x 32 consecutive fp32 columns of TMEM into 32 registers per thread.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor (tcgen05 "smem descriptor"): start address, leading and
-// stride byte offsets (all >> 4), version 1 at bit 46, 128-byte swizzle (layout 2) at bit 61.
-__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3fff);
-  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3fff) << 16;
-  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3fff) << 32;
-  d |= 1ull << 46;
-  d |= 2ull << 61;
-  return d;
-}
+using namespace tc;
 
 // Descriptor of one UMMA_K slice (k-th, 16 elements) of a stage operand with `rows` MN rows.
 // K-major tile: rows of 128 bytes (64 K elements), 8-row groups 1024 bytes apart; advancing K
@@ -154,6 +50,7 @@ struct GemmArgs {
   int64_t m, n, k, batch;
   int tiles_m, tiles_n;
   int sym;                 // symmetric output: only tiles meeting the upper triangle, mirrored
+  int m_fastest;           // tile order walks M first: the (larger) N-side operand streams once
   int64_t tiles_per_batch;
   int64_t num_tiles;
   int num_kb;
@@ -240,8 +137,13 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int64_t t, int64_
   b = t / g.tiles_per_batch;
   int64_t r = t - b * g.tiles_per_batch;
   if (!g.sym) {
-    tm = static_cast<int>(r / g.tiles_n);
-    tn = static_cast<int>(r - static_cast<int64_t>(tm) * g.tiles_n);
+    if (g.m_fastest) {
+      tn = static_cast<int>(r / g.tiles_m);
+      tm = static_cast<int>(r - static_cast<int64_t>(tn) * g.tiles_m);
+    } else {
+      tm = static_cast<int>(r / g.tiles_n);
+      tn = static_cast<int>(r - static_cast<int64_t>(tm) * g.tiles_n);
+    }
     return;
   }
   int row = 0;
@@ -428,24 +330,11 @@ ns_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 
 // ------------------------------------------------------------------ host side
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 // 3-D bf16 tensor map over [batch][rows][inner] with leading dim `ld` and batch stride `bs`
 // (elements); box = box_inner x box_rows x 1 with 128-byte swizzle and zero fill out of bounds.
 int encode_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t batch, int64_t ld,
                int64_t bs, int box_inner, int box_rows) {
-  auto fn = get_encode_fn();
+  auto fn = encode_fn();
   if (fn == nullptr) return MUZO_ERR_UNSUPPORTED;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(batch)};
@@ -523,6 +412,10 @@ int muzo_ns_gemm(const void* a, int64_t lda, int64_t a_batch_stride, int a_mn, c
   g.tiles_m = static_cast<int>((m + BM - 1) / BM);
   g.tiles_n = static_cast<int>((n + BN - 1) / BN);
   g.sym = symmetric ? 1 : 0;
+  // Concurrent CTAs share the operand of the fast tile index: walking M first keeps the N-side
+  // operand's column block hot and streams it from DRAM once when it is the larger operand
+  // (B X with X = m x n, n > m); otherwise N first.
+  g.m_fastest = (!g.sym && n > m) ? 1 : 0;
   if (g.sym) {
     g.tiles_per_batch = 0;
     for (int tm = 0; tm < g.tiles_m; ++tm) g.tiles_per_batch += g.tiles_n - (tm * BM) / BN;

@@ -5,9 +5,16 @@
 // Maxima are accumulated as order-preserving integers with atomicMax, then decoded; the eager
 // rounding of the logits, round(round(q.k) * scale) in the model dtype, is monotonic, so it is
 // applied once to the maximum dot product instead of to every logit.
+#include <cstdlib>
+
 #include "muzo_common.cuh"
 
 namespace muzo {
+
+int qk_max_tensor_cores(const void* q, const void* k, int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t sq,
+                        int64_t sk, int64_t d, int64_t qsb, int64_t qsh, int64_t qss, int64_t ksb, int64_t ksh,
+                        int64_t kss, int causal, int* enc, int32_t* valid, cudaStream_t stream);
+
 namespace {
 
 __device__ __forceinline__ int encode_max(float f) {
@@ -144,6 +151,16 @@ logits_head_max_kernel(const char* __restrict__ logits, int64_t bsz, int64_t hea
   if (!finite) atomicExch(valid, 0);
 }
 
+// The tensor-core path can be turned off for comparison runs (MUZO_QK_SIMT=1).
+bool qk_tensor_cores_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* e = getenv("MUZO_QK_SIMT");
+    enabled = (e != nullptr && e[0] == '1') ? 0 : 1;
+  }
+  return enabled == 1;
+}
+
 __global__ void max_merge_kernel(float* running, const float* fresh, const int32_t* valid, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -169,7 +186,20 @@ int muzo_qk_max(const void* q, const void* k, int dtype, int64_t batch, int64_t 
   int* enc = reinterpret_cast<int*>(smax);
   init_max_kernel<<<static_cast<unsigned>((hq + 255) / 256), 256, 0, s>>>(enc, static_cast<int>(hq), d_valid);
   const int64_t units = batch * hq * ((seq_q + QT - 1) / QT);
-  if (units > 0 && seq_k > 0) {
+  // bf16 / fp16 with TMA-compatible strides (multiples of 8 elements, 16-byte aligned bases)
+  // run on the tensor cores; fp32 (exact fp32 products, as the reference's fp32 matmul) and
+  // other layouts on the CUDA cores
+  const bool tensor_path = (dtype == MUZO_BF16 || dtype == MUZO_F16) && head_dim % 8 == 0 &&
+                           q_stride_b % 8 == 0 && q_stride_h % 8 == 0 && q_stride_s % 8 == 0 &&
+                           k_stride_b % 8 == 0 && k_stride_h % 8 == 0 && k_stride_s % 8 == 0 &&
+                           (reinterpret_cast<uintptr_t>(q) & 15u) == 0 && (reinterpret_cast<uintptr_t>(k) & 15u) == 0 &&
+                           batch <= 0x7fffffffLL && hq <= 0x7fffffffLL && seq_q <= 0x7fffffffLL &&
+                           seq_k <= 0x7fffffffLL && qk_tensor_cores_enabled();
+  if (tensor_path && units > 0 && seq_k > 0) {
+    const int st = qk_max_tensor_cores(q, k, dtype, batch, hq, hkv, seq_q, seq_k, head_dim, q_stride_b, q_stride_h,
+                                       q_stride_s, k_stride_b, k_stride_h, k_stride_s, causal, enc, d_valid, s);
+    if (st != MUZO_OK) return st;
+  } else if (units > 0 && seq_k > 0) {
     if (units > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;
     const unsigned grid = static_cast<unsigned>(units);
     const char* qp = static_cast<const char*>(q);

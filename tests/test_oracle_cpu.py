@@ -169,3 +169,17 @@ def test_partition_balances_llama_layers():
         loads = [sum(c for c, o in zip(costs, owner) if o == r) for r in range(world)]
         assert max(loads) / min(loads) < 1.02, (world, loads)
         assert partition_blocks(costs, world) == owner  # deterministic on every rank
+
+
+def test_philox_published_known_answers():
+    """Philox4x32-10 against the known-answer vectors published with the Random123 library
+    (Salmon et al., SC'11): zero counter/key, all-ones counter/key, and the pi-digits case."""
+    cases = [
+        ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+        ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+        ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+         (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+    ]
+    for ctr, key, want in cases:
+        words = orc.philox4x32_10(*(np.array([c], np.uint64) for c in ctr), key[0] | (key[1] << 32))
+        assert tuple(int(w[0]) for w in words) == want

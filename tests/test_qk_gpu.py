@@ -20,7 +20,8 @@ def _ulp(x: torch.Tensor, bits: int) -> torch.Tensor:
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("b,hq,hkv,sq,sk,d", [(2, 8, 2, 100, 100, 64), (1, 4, 4, 64, 64, 128), (2, 6, 1, 33, 70, 32)])
+@pytest.mark.parametrize("b,hq,hkv,sq,sk,d", [(2, 8, 2, 100, 100, 64), (1, 4, 4, 64, 64, 128), (2, 6, 1, 33, 70, 32),
+                                             (1, 8, 2, 1000, 1000, 128), (1, 2, 1, 300, 700, 96)])
 def test_qk_max_matches_eager_logits(device, dtype, causal, b, hq, hkv, sq, sk, d):
     from muzo_clip_b200 import _qk
 
@@ -34,7 +35,7 @@ def test_qk_max_matches_eager_logits(device, dtype, causal, b, hq, hkv, sq, sk, 
     torch.cuda.synchronize()
     assert int(valid.item()) == 1
     got = got.cpu()
-    bits = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 21}[dtype]
+    bits = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 19}[dtype]
     assert bool(((got - ref).abs() <= _ulp(ref, bits)).all()), (got, ref)
 
 
@@ -122,7 +123,7 @@ def test_probe_and_apply_matches_reference(device, dtype):
     twin = copy.deepcopy(model)
     ids = torch.randint(0, 1024, (4, 64), generator=torch.Generator().manual_seed(1)).to(device)
     ref_smax = _reference_capture(twin, ids)
-    tau, alpha = 20.0, 0.5
+    tau, alpha = 5.0, 0.5
     opt = MuZOClipOptimizer(model, enable_qk_clip=True, qk_clip_tau=tau, qk_clip_alpha=alpha)
     # capture only, to compare the maxima before any scaling
     ctrl = opt.qk_clip
@@ -131,7 +132,8 @@ def test_probe_and_apply_matches_reference(device, dtype):
         with ctrl.capture():
             with torch.no_grad():
                 model(input_ids=ids)
-    bits = 7 if dtype == torch.bfloat16 else 21
+    # bf16: one ulp (rounding of the same dot product); fp32: a few ulps of accumulation order
+    bits = 7 if dtype == torch.bfloat16 else 19
     assert set(ctrl._captured_smax) == set(ref_smax)
     for name, ref in ref_smax.items():
         got = ctrl._captured_smax[name].cpu()
@@ -152,7 +154,8 @@ def test_probe_and_apply_matches_reference(device, dtype):
         if "q_proj" in n1 or "k_proj" in n1:
             diff = (p1.float() - p2.float()).abs()
             assert bool((diff <= _ulp(p2.float(), bits)).all()), n1
-            assert (p1 == p2).float().mean().item() > 0.99
+            if dtype == torch.bfloat16:  # factors rounded to bf16 coincide almost always
+                assert (p1 == p2).float().mean().item() > 0.99
         else:
             assert torch.equal(p1, p2), n1
 
