@@ -1,0 +1,78 @@
+"""End to end on the tiny Llama of the reference's first benchmark configuration: 2 layers,
+hidden 256, 4 heads, MLP 688, vocab 1024, fp32, batch 4 x seq 64 token ids, README defaults,
+normal noise, 20 SPSA steps and one QK-Clip probe — the README's sanity checks
+(README.md:253-258) plus agreement of every update with the reference path."""
+
+from __future__ import annotations
+
+import copy
+import math
+
+import pytest
+import torch
+
+import torch_reference as tr
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(device, attn="eager"):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(1234)
+    cfg = LlamaConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=4,
+                      intermediate_size=688, vocab_size=1024, attn_implementation=attn, initializer_range=0.02)
+    return LlamaForCausalLM(cfg).float().to(device)
+
+
+def test_tiny_llama_twenty_steps_and_probe(device):
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = _model(device)
+    ids = torch.randint(0, 1024, (4, 64), generator=torch.Generator().manual_seed(0)).to(device)
+    opt = MuZOClipOptimizer(model, enable_qk_clip=True, seed=1234)
+    assert len(opt.selected_parameter_names()) == 14
+
+    def closure():
+        return model(input_ids=ids, labels=ids).loss
+
+    projections, steps = [], []
+    twin = copy.deepcopy(model)
+    named_twin = [(n, p) for n, p in twin.named_parameters() if n in set(opt.selected_parameter_names())]
+    max_rel = 0.0
+    for _ in range(20):
+        proj = opt.estimate_projection(closure)
+        projections.append(proj)
+        # the reference path's perturb / restore sweep on the twin: +eps, -2eps, +eps
+        for s in (1.0, -2.0, 1.0):
+            tr.perturb(named_twin, proj["seed"], s, opt.zo_eps, "normal")
+        before = [p.detach().clone() for _, p in named_twin]
+        st = opt.step()
+        steps.append(st)
+        if not st["skipped"]:
+            ref = tr.step(named_twin, list(opt.history), lr=st["lr"], beta=opt.beta_momentum, ns_steps=opt.ns_steps,
+                          muon_scale=opt.muon_scale, ratio_clip=opt.update_ratio_clip,
+                          weight_decay=opt.weight_decay, distribution="normal")
+            assert ref["updated_param_count"] == st["updated_param_count"]
+            for (n, p), b in zip(named_twin, before):
+                mine = dict(model.named_parameters())[n].detach()
+                d_ref, d_mine = p.detach() - b, mine - b
+                rel = (d_mine - d_ref).norm() / d_ref.norm().clamp_min(1e-30)
+                max_rel = max(max_rel, rel.item())
+            # keep both on the same weights so each step is compared from a common start
+            with torch.no_grad():
+                for (n, p) in named_twin:
+                    p.copy_(dict(model.named_parameters())[n].detach())
+    # fp32 weights: each update within the Newton-Schulz accumulation-order tolerance
+    assert max_rel < 6e-2, max_rel
+    losses = [p["loss_plus"] for p in projections]
+    assert all(math.isfinite(x) for x in losses)
+    used = [p["p_used"] for p in projections if not p["skipped"]]
+    assert used and not all(abs(abs(u) - 3.0) < 1e-9 for u in used)          # not glued to +-3
+    applied = [s for s in steps if not s["skipped"]]
+    assert len(applied) >= 10
+    assert all(s["update_ratio_max"] <= opt.update_ratio_clip * (1 + 1e-3) for s in applied)
+    assert steps[0]["skip_reason"] == "waiting for min_history=4"
+    qk = opt.probe_and_apply_qk_clip(closure, force_eager=True)
+    assert qk["enabled"] and qk["exact_logits"] and qk["qk_smax_max"] > 0.0
+    assert set(qk) == {"enabled", "exact_logits", "fallback_used", "disabled_reason", "qk_smax_max", "qk_clip_count"}

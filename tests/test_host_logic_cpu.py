@@ -143,3 +143,32 @@ def test_cpu_tensors_are_rejected_not_computed():
         zeropower_via_newtonschulz5(torch.ones(4, 4))
     with pytest.raises(TypeError):
         make_zo_noise_like(torch.zeros(4, 4, dtype=torch.int32), 1, "w")
+
+
+def test_state_dict_resumes_identically(monkeypatch):
+    """Resume format (the reference keeps this state only in memory): a restored optimizer
+    continues with the same seeds, projections and statistics as the uninterrupted one."""
+    import json
+
+    import muzo_clip_b200.muzo_optimizer as mo
+
+    monkeypatch.setattr(mo, "StepEngine", FakeEngine)
+    kw = dict(lr=1e-3, seed=21, horizon=5, min_history=2)
+    a = mo.MuZOClipOptimizer(_model(), **kw)
+    closure = _closure(LOSSES)
+    for _ in range(5):
+        a.estimate_projection(closure)
+        a.step()
+    saved = json.loads(json.dumps(a.state_dict()))  # must survive a JSON round trip
+    b = mo.MuZOClipOptimizer(_model(), **kw)
+    b.load_state_dict(saved)
+    rest = LOSSES[5:]
+    ca, cb = _closure(rest), _closure(rest)
+    for _ in rest:
+        pa, pb = a.estimate_projection(ca), b.estimate_projection(cb)
+        assert {k: v for k, v in pa.items() if not (isinstance(v, float) and math.isnan(v))} == \
+            {k: v for k, v in pb.items() if not (isinstance(v, float) and math.isnan(v))}
+        assert a.step() == b.step()
+    with pytest.raises(ValueError):
+        c = mo.MuZOClipOptimizer(torch.nn.Linear(4, 4), **kw)
+        c.load_state_dict(saved)
