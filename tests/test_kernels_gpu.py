@@ -193,21 +193,30 @@ def _gemm_case(device, m, n, k, batch, a_mn, b_mn, epi):
     assert bad == 0, f"{bad} mismatches, max err {err.max().item()}"
 
 
+@pytest.fixture(params=["pair", "single"])
+def gemm_kernel(request, monkeypatch):
+    """Outputs of at least 256 x 256 run on the CTA-pair kernel (256 x 256 tiles over two SMs)
+    unless MUZO_GEMM_PAIR=0 selects the one-SM kernel (128 x 256 tiles): both are checked."""
+    monkeypatch.setenv("MUZO_GEMM_PAIR", "1" if request.param == "pair" else "0")
+    return request.param
+
+
 @pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("epi", [0, 1, 2])
-def test_ns_gemm_variants(device, a_mn, b_mn, epi):
+def test_ns_gemm_variants(device, gemm_kernel, a_mn, b_mn, epi):
     _gemm_case(device, 256, 512, 320, 2, a_mn, b_mn, epi)
 
 
-@pytest.mark.parametrize("m,n,k,batch", [(128, 256, 64, 1), (300, 696, 200, 3), (64, 40, 24, 2), (1024, 1024, 4096, 1)])
-def test_ns_gemm_shapes(device, m, n, k, batch):
+@pytest.mark.parametrize("m,n,k,batch", [(128, 256, 64, 1), (300, 696, 200, 3), (64, 40, 24, 2), (1024, 1024, 4096, 1),
+                                         (257, 1000, 72, 2), (520, 264, 136, 1)])
+def test_ns_gemm_shapes(device, gemm_kernel, m, n, k, batch):
     for a_mn, b_mn in ((0, 0), (0, 1), (1, 1)):
         _gemm_case(device, m, n, k, batch, a_mn, b_mn, 2)
 
 
 @pytest.mark.parametrize("m,k,batch,tall", [(512, 384, 2, False), (1024, 4096, 1, False), (300, 200, 2, True),
-                                            (256, 688, 1, True)])
-def test_ns_gemm_symmetric_outputs(device, m, k, batch, tall):
+                                            (256, 688, 1, True), (776, 136, 1, False)])
+def test_ns_gemm_symmetric_outputs(device, gemm_kernel, m, k, batch, tall):
     """Symmetric mode: X X^T (wide, K-major) or G^T G (tall, MN-major), then b A + c A A, each
     computed on upper-triangle tiles and mirrored. The result must be exactly symmetric and its
     upper triangle bit-equal to the full computation."""
