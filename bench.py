@@ -144,6 +144,22 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+# DRAM traffic measured by one ncu capture of this workload on one B200 (1-pass metrics
+# gpu__time_duration.sum, dram__bytes_read.sum, dram__bytes_write.sum, --clock-control none, on
+# `python bench.py --steps 1 --warmup 1 --no-cpu-baseline`): read + write summed over the 105
+# ns_gemm launches of one step (960.3 GB over the 2 captured steps), and per perturbation pass.
+NS_DRAM_BYTES_PER_STEP = 480.2e9
+PERTURB_DRAM_BYTES_PER_PASS = 27.86e9
+
+
+def ns_operand_bytes(rows: int, cols: int, steps: int = 5) -> float:
+    """Minimal DRAM bytes of the Newton-Schulz GEMMs for one matrix: per iteration X read and A
+    written (X X^T), A read and B written (b A + c A A), B and X read and X written (a X + B X),
+    each once: 6 m n + 8 m^2 bytes in bf16, m = min(rows, cols), n = max."""
+    m, n = min(rows, cols), max(rows, cols)
+    return steps * (6.0 * m * n + 8.0 * m * m)
+
+
 def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -294,6 +310,7 @@ def run_gpu(args) -> int:
         peaks = load_peaks()
         clk = clocks.summary()
         n_elems = total_numel(args.layers)
+        ns_bytes_min = sum(ns_operand_bytes(b.rows, b.cols) for b in engine.owned)
         h2d = 8 * len(engine.blocks) * 3 + 8 * len(engine.owned) * HORIZON + 4 * HORIZON
         d2h = engine.state_bytes + 16
         line = {
@@ -321,7 +338,7 @@ def run_gpu(args) -> int:
             "ns_tflops": round(ns_tflops, 1),
             "roofline": {
                 "bound": "tensor",
-                "kernel": "ns_gemm_kernel (Newton-Schulz GEMMs; all launches of the timed steps)",
+                "kernel": "ns_gemm_pair_kernel / ns_gemm_kernel (Newton-Schulz GEMMs; all launches of the timed steps)",
                 "achieved": round(ns_tflops, 1),
                 "peak": peaks["bf16_tflops_sustained"],
                 "unit": "TFLOP/s",
@@ -330,12 +347,16 @@ def run_gpu(args) -> int:
                 "executed_tflops": round(ns_exec_tflops, 1),
                 "executed_frac": round(ns_exec_tflops / peaks["bf16_tflops_sustained"], 4),
                 "peak_source": f"{peaks['source']} bf16 sustained",
-                "traffic": None,
+                "traffic": NS_DRAM_BYTES_PER_STEP if world == 1 else None,
+                "traffic_unit": "DRAM bytes per step, all ns_gemm launches (ncu capture of this workload, 1 GPU)",
+                "operand_bytes": round(ns_bytes_min),
             },
             "perturb_roofline": {
                 "bound": "hbm", "achieved": round(perturb_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(perturb_gbs / peaks["hbm_gbs"], 4), "peak_source": f"{peaks['source']} copy",
                 "rademacher_achieved": round(rad_gbs, 1), "rademacher_frac": round(rad_gbs / peaks["hbm_gbs"], 4),
+                "traffic": PERTURB_DRAM_BYTES_PER_PASS, "traffic_unit": "DRAM bytes per pass (ncu)",
+                "algorithmic_bytes": perturb_bytes,
             },
             "e2e": {"value": round(wall_ms, 3), "unit": "ms/step", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
@@ -384,18 +405,58 @@ def run_reference(args) -> int:
 # Newton-Schulz (batch of 8 per shape) and bandwidth (1 M - 2 G elements, horizon 1-16) sweeps.
 
 
-def _event_ms(fn, reps: int, stream) -> float:
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
+L2_FLUSH_BYTES = 512 << 20   # written between timed iterations whose working set could stay in L2
+
+
+def _event_ms(fn, reps: int, stream, flush: torch.Tensor | None = None) -> float:
+    """Mean device time of fn over reps; with `flush`, the buffer is rewritten before each
+    iteration (outside the timed interval) so that every iteration starts from a cold L2."""
+    if flush is None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in ev:
+        flush.add_(1)
+        a.record(stream)
         fn()
-    e1.record(stream)
+        b.record(stream)
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / reps
+    return sum(a.elapsed_time(b) for a, b in ev) / reps
+
+
+SWEEPS = {
+    # Newton-Schulz, batch of 8 per shape (rows x cols)
+    "ns": [(1024, 1024), (4096, 4096), (4096, 14336), (14336, 4096), (8192, 28672)],
+    # perturbation pass over flat bf16 tensors [numel / 4096, 4096]
+    "perturb": [1 << 20, 16 << 20, 256 << 20, 1 << 30, 2 << 30],
+    # momentum rebuild horizons
+    "rebuild": [1, 2, 4, 8, 16],
+}
 
 
 def run_case(args) -> int:
+    if not args.sweep:
+        return _run_one_case(args)
+    for v in SWEEPS[args.case] if args.case in SWEEPS else [None]:
+        a = argparse.Namespace(**vars(args))
+        if args.case == "ns":
+            a.rows, a.cols, a.batch = v[0], v[1], 8
+        elif args.case == "perturb":
+            a.numel = v
+        elif args.case == "rebuild":
+            a.horizon = v
+        _run_one_case(a)
+        torch.cuda.empty_cache()
+    return 0
+
+
+def _run_one_case(args) -> int:
     from muzo_clip_b200 import _lib
     from muzo_clip_b200._engine import ns_flops
     from muzo_clip_b200.newton_schulz import allocate_ns_buffers, ns_iterations
@@ -444,10 +505,15 @@ def run_case(args) -> int:
             nbytes = 4.0 * numel  # bf16(M) write + W read
         for _ in range(args.warmup):
             run()
-        ms = _event_ms(run, args.steps, stream)
+        # working sets below 1 GiB (8 x the 126 MB L2) could be partly served from L2 on repeated
+        # passes: flush between them
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device) if nbytes < 2 * L2_FLUSH_BYTES \
+            else None
+        ms = _event_ms(run, args.steps, stream, flush)
         gbs = nbytes / (ms * 1e-3) / 1e9
         out.update(numel=numel, dist=args.dist, horizon=args.horizon if args.case == "rebuild" else None,
-                   ms=round(ms, 4), gbs=round(gbs, 1), hbm_frac=round(gbs / peaks["hbm_gbs"], 4))
+                   ms=round(ms, 4), gbs=round(gbs, 1), hbm_frac=round(gbs / peaks["hbm_gbs"], 4),
+                   l2="flushed between passes" if flush is not None else "working set larger than L2")
     elif args.case == "qk":
         # per-head max logit of one attention layer: Q [B, Hq, S, D], K [B, Hkv, S, D] as the
         # transposed views of [B, S, H, D] that transformers passes to attention functions
@@ -490,6 +556,8 @@ def main() -> int:
     ap.add_argument("--impl", default="muzo", choices=["muzo", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="with --case: ns = 5 shapes x batch 8; perturb = 1 M..2 G elements; rebuild = horizon 1..16")
     args = ap.parse_args()
     if args.case is not None:
         return run_case(args)

@@ -66,6 +66,25 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Two values rounded to bf16 and back through one packed conversion: the same round-to-nearest-
+// even result as two bf16r calls, on the ALU pipe instead of one conversion each on the XU pipe.
+__device__ __forceinline__ void bf16r2(float& a, float& b) {
+  const uint32_t p = pack_bf16(a, b);
+  a = bf16_lo(p);
+  b = bf16_hi(p);
+}
+
+// Pairwise round_to.
+__device__ __forceinline__ void round2_to(float& a, float& b, int dtype) {
+  if (dtype == MUZO_BF16) {
+    bf16r2(a, b);
+  } else if (dtype == MUZO_F16) {
+    const __half2 h = __floats2half2_rn(a, b);
+    a = __low2float(h);
+    b = __high2float(h);
+  }
+}
+
 __device__ __forceinline__ float half_lo(uint32_t packed) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(packed & 0xffffu)));
 }

@@ -225,7 +225,9 @@ perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
           float w[8];
           load8(sv.param, li, DTYPE, w);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w[k]);
+          for (int k = 0; k < 8; k += 2) round2_to(z[j][k], z[j][k + 1], DTYPE);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, z[j][k], w[k]);
           store8(sv.param, li, DTYPE, w);
         } else {
           for (int k = 0; k < 8 && li + k < sv.numel; ++k) {
@@ -279,11 +281,13 @@ __device__ __forceinline__ void accumulate4x4(uint64_t key, uint64_t t0, uint64_
     if (DIST == MUZO_NORMAL) {
       curandStatePhilox4_32_10_t st;
       curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
-      const float4 n = curand_normal4(&st);
-      acc[0][k] = __fmaf_rn(alpha, round_to(n.x, PDTYPE), acc[0][k]);
-      acc[1][k] = __fmaf_rn(alpha, round_to(n.y, PDTYPE), acc[1][k]);
-      acc[2][k] = __fmaf_rn(alpha, round_to(n.z, PDTYPE), acc[2][k]);
-      acc[3][k] = __fmaf_rn(alpha, round_to(n.w, PDTYPE), acc[3][k]);
+      float4 n = curand_normal4(&st);
+      round2_to(n.x, n.y, PDTYPE);
+      round2_to(n.z, n.w, PDTYPE);
+      acc[0][k] = __fmaf_rn(alpha, n.x, acc[0][k]);
+      acc[1][k] = __fmaf_rn(alpha, n.y, acc[1][k]);
+      acc[2][k] = __fmaf_rn(alpha, n.z, acc[2][k]);
+      acc[3][k] = __fmaf_rn(alpha, n.w, acc[3][k]);
     } else {
       // z = +-1 is exact in every dtype and alpha * z is exact: acc + alpha*z == acc +- alpha
       const uint4 r = thread_words(key, t0 + k, word_offset, trip);
@@ -360,11 +364,14 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
         for (int k = 0; k < cnt; ++k) store_elem(sv.out, li + k, MUZO_BF16, m[k]);
       }
       float pm = 0.0f, px = 0.0f, pw = 0.0f;
+      float mb[4] = {m[0], m[1], m[2], m[3]};
+      bf16r2(mb[0], mb[1]);
+      bf16r2(mb[2], mb[3]);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         if (k < cnt) {
           finite = finite && isfinite(m[k]);
-          const float xb = bf16r(m[k]);
+          const float xb = mb[k];
           pm = __fmaf_rn(m[k], m[k], pm);
           px = __fmaf_rn(xb, xb, px);
           pw = __fmaf_rn(w[k], w[k], pw);

@@ -1,5 +1,5 @@
 // Newton-Schulz GEMMs for MuZO-Clip on sm_100a: tcgen05.mma with fp32 accumulators in TMEM,
-// operands staged in shared memory by TMA (cp.async.bulk.tensor, no multicast), and the
+// operands staged in shared memory by TMA tensor copies (each CTA fills only its own tiles), and the
 // element-wise parts of the quintic iteration (newton_schulz.py:55-58) fused into the epilogue.
 //
 // Two kernels share the tile enumeration and the epilogue: the CTA-pair kernel (256 x 256 tiles,
@@ -95,15 +95,21 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, int64_t b, int
 #pragma unroll
       for (int i = 0; i < 32; ++i) e[i] = col0 + i < g.n ? __bfloat162float(g.e[base + i]) : 0.0f;
     }
+    // roundings in pairs (one packed conversion per two values)
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float a = __uint_as_float(acc[i]);
-      const float t1 = bf16r(g.c1 * e[i]);           // c1 * E, rounded to bf16
+    for (int i = 0; i < 32; i += 2) {
+      float a0 = __uint_as_float(acc[i]), a1 = __uint_as_float(acc[i + 1]);
+      float t0 = g.c1 * e[i], t1 = g.c1 * e[i + 1];
+      bf16r2(t0, t1);                                  // c1 * E, rounded to bf16
+      bf16r2(a0, a1);                                  // bf16(A @ A) or bf16(B @ X)
       if (EPI == MUZO_EPI_POLY) {
-        const float t2 = bf16r(g.c2 * bf16r(a));     // c2 * bf16(A @ A)
-        o[i] = t1 + t2;
+        float u0 = g.c2 * a0, u1 = g.c2 * a1;
+        bf16r2(u0, u1);                                // c2 * bf16(A @ A)
+        o[i] = t0 + u0;
+        o[i + 1] = t1 + u1;
       } else {
-        o[i] = t1 + bf16r(a);                        // a*X + bf16(B @ X)
+        o[i] = t0 + a0;                                // a*X + bf16(B @ X)
+        o[i + 1] = t1 + a1;
       }
     }
   }

@@ -1,5 +1,5 @@
 // Device helpers shared by the tcgen05 kernels: mbarriers with bounded waits, TMA tensor loads
-// (no multicast), tcgen05 fences / commit / MMA / TMEM loads, shared-memory matrix descriptors,
+// (each CTA fills only its own shared memory), tcgen05 fences / commit / MMA / TMEM loads, shared-memory matrix descriptors,
 // and host-side tensor-map encoding through the driver entry point.
 #pragma once
 

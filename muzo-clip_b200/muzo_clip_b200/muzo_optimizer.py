@@ -173,6 +173,7 @@ class MuZOClipOptimizer:
         self._has_pending_update = False
         self._last_step_updated = False
         self._engine: StepEngine | None = None
+        self._snapshot_bufs: list[torch.Tensor] | None = None
 
         self.qk_clip: QKClipController | None = None
         if enable_qk_clip:
@@ -409,12 +410,31 @@ class MuZOClipOptimizer:
 
     @torch.no_grad()
     def _snapshot_selected_params(self):
-        return [(s.param, s.param.detach().cpu().clone()) for s in self.selected_params]
+        """Host copy of every selected parameter for `rollback` / `restore_exact`
+        (muzo_optimizer.py:482-483). The copies land in page-locked buffers allocated on first use
+        and reused afterwards, as asynchronous device-to-host copies on the current stream: the
+        perturbation kernels launched next on that stream start after the copies have read the
+        weights, so the host never waits. Without page-locked memory the buffers are pageable and
+        the copies synchronous."""
+        if self._snapshot_bufs is None:
+            bufs = []
+            for s in self.selected_params:
+                try:
+                    bufs.append(torch.empty(s.param.shape, dtype=s.param.dtype, pin_memory=True))
+                except RuntimeError:
+                    bufs.append(torch.empty(s.param.shape, dtype=s.param.dtype))
+            self._snapshot_bufs = bufs
+        snapshot = []
+        for s, buf in zip(self.selected_params, self._snapshot_bufs):
+            buf.copy_(s.param.detach(), non_blocking=True)
+            snapshot.append((s.param, buf))
+        return snapshot
 
     @torch.no_grad()
     def _restore_snapshot(self, snapshot) -> None:
+        """Copy the snapshot back (muzo_optimizer.py:486-488), host-to-device on the current stream."""
         for param, saved in snapshot:
-            param.data.copy_(saved.to(device=param.device, dtype=param.dtype))
+            param.data.copy_(saved, non_blocking=True)
 
     @torch.no_grad()
     def _restore_after_failed_projection(self, seed: int, displacement: int, snapshot) -> None:

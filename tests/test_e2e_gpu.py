@@ -76,3 +76,44 @@ def test_tiny_llama_twenty_steps_and_probe(device):
     qk = opt.probe_and_apply_qk_clip(closure, force_eager=True)
     assert qk["enabled"] and qk["exact_logits"] and qk["qk_smax_max"] > 0.0
     assert set(qk) == {"enabled", "exact_logits", "fallback_used", "disabled_reason", "qk_smax_max", "qk_clip_count"}
+
+
+def _selected(model, opt):
+    names = set(opt.selected_parameter_names())
+    return {n: p.detach().clone() for n, p in model.named_parameters() if n in names}
+
+
+def test_restore_exact_and_rollback_restore_bitwise(device):
+    """restore_exact replaces the +eps restore pass with the host snapshot (muzo_optimizer.py:208-211)
+    and rollback restores it when the projection is rejected (218-221): in bf16 both must give the
+    weights back bit for bit, through the page-locked snapshot buffers."""
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = _model(device).to(torch.bfloat16)
+    ids = torch.randint(0, 1024, (2, 32), generator=torch.Generator().manual_seed(1)).to(device)
+
+    def closure():
+        return model(input_ids=ids, labels=ids).loss
+
+    opt = MuZOClipOptimizer(model, restore_exact=True, seed=7)
+    for _ in range(2):
+        before = _selected(model, opt)
+        proj = opt.estimate_projection(closure)
+        assert not proj["skipped"]
+        after = _selected(model, opt)
+        assert all(torch.equal(before[n], after[n]) for n in before)
+    assert opt._snapshot_bufs is not None and opt._snapshot_bufs[0].is_pinned()
+
+    calls = {"n": 0}
+
+    def bad_closure():
+        calls["n"] += 1
+        return float("nan") if calls["n"] == 2 else closure()
+
+    opt = MuZOClipOptimizer(model, rollback=True, seed=9)
+    before = _selected(model, opt)
+    proj = opt.estimate_projection(bad_closure)
+    assert proj["skipped"] and proj["skip_reason"] is not None
+    after = _selected(model, opt)
+    assert all(torch.equal(before[n], after[n]) for n in before)
+    assert not opt.history
