@@ -4,9 +4,9 @@ Every rank keeps a full replica of the selected weights. Perturbation needs no c
 the noise of a block is a pure function of (seed, name, shape, block index), so all ranks
 perturb their replicas identically. The step is partitioned: blocks are assigned to ranks by
 Newton-Schulz FLOPs (LPT greedy, identical on every rank); each rank rebuilds, orthogonalises
-and applies only its blocks, and after each shape class the owners broadcast the updated blocks
-with NCCL — asynchronously, on NCCL's stream, so the transfer of class c overlaps the GEMMs of
-class c + 1. Per-block statistics are combined with one small all-reduce.
+and applies only its blocks, and once its last GEMM is queued the owners broadcast the updated
+blocks with NCCL, all in one group, on NCCL's stream; the compute stream waits for them before
+the next use of the weights. Per-block statistics are combined with one small all-reduce.
 """
 
 from __future__ import annotations
@@ -24,18 +24,17 @@ class ShardedStepEngine(StepEngine):
         rank = dist.get_rank(process_group)
         world = dist.get_world_size(process_group)
         super().__init__(opt, rank=rank, world=world, process_group=process_group)
-        self._works: list = []
+        self._pending: list = []
         self._global_ranks = [dist.get_global_rank(process_group, r) if process_group is not None else r
                               for r in range(world)] if process_group is not None else list(range(world))
 
     def _after_class(self, class_key) -> None:
-        if self.world <= 1:
-            return
-        for b in self.blocks:
-            if (b.rows, b.cols, self._code(b)) != class_key:
-                continue
-            src = self._global_ranks[self.owner[b.index]]
-            self._works.append(dist.broadcast(b.tensor, src=src, group=self.group, async_op=True))
+        """Record that the blocks of `class_key` are final on their owners. The transfers start in
+        `_finish_collectives`, after the last GEMM: NCCL kernels running next to the persistent
+        Newton-Schulz GEMMs hold SMs that the GEMMs' statically scheduled CTAs then wait for
+        (measured on 2 B200s: 378 ms per step with per-class overlap, 361 ms deferred)."""
+        if self.world > 1:
+            self._pending.append(class_key)
 
     @staticmethod
     def _code(b) -> int:
@@ -44,9 +43,24 @@ class ShardedStepEngine(StepEngine):
         return _lib.dtype_code(b.dtype)
 
     def _finish_collectives(self) -> None:
-        works, self._works = self._works, []
+        """Broadcast every owned block from its owner, all classes in one NCCL group (the ranks
+        take the same classes in the same order), and make the current stream wait for them."""
+        pending, self._pending = self._pending, []
+        if not pending:
+            return
+        todo = [b for ck in pending for b in self.blocks if (b.rows, b.cols, self._code(b)) == ck]
+        backend = dist.get_backend(self.group)
+        manager = getattr(dist, "_coalescing_manager", None)
+        if backend == "nccl" and manager is not None:
+            with manager(group=self.group, device=self.device, async_ops=True) as cm:
+                for b in todo:
+                    dist.broadcast(b.tensor, src=self._global_ranks[self.owner[b.index]], group=self.group)
+            cm.wait()
+            return
+        works = [dist.broadcast(b.tensor, src=self._global_ranks[self.owner[b.index]], group=self.group,
+                                async_op=True) for b in todo]
         for w in works:
-            w.wait()  # makes the current stream wait for NCCL's; no host block
+            w.wait()
 
     def gather_stats(self, per_block: dict[int, dict]) -> dict[int, dict]:
         """Combine the owners' per-block statistics on every rank (sum all-reduce)."""

@@ -51,7 +51,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
 
         eng = Fake()
         eng.blocks, eng.owner, eng.world, eng.group = blocks, owner, world, dist.group.WORLD
-        eng._works, eng._global_ranks, eng.device = [], list(range(world)), torch.device("cpu")
+        eng._pending, eng._global_ranks, eng.device = [], list(range(world)), torch.device("cpu")
         # owners "update" their blocks; everyone else holds stale values
         for b in blocks:
             if owner[b.index] == rank:

@@ -1,0 +1,88 @@
+"""The sharded step on 2 GPUs (NCCL, one process per GPU) against one GPU.
+
+Every rank perturbs its own replica; each block is rebuilt, orthogonalised and applied by its
+owner only and broadcast to the others. With the same seeds and losses the weights must come out
+bit-identical on both ranks and equal to the single-GPU run: the kernels work per matrix, so the
+partition and the batch composition change nothing. Skipped with fewer than 2 GPUs.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+SHAPES = [(512, 256), (256, 512), (1024, 256), (384, 384), (256, 768), (768, 256), (512, 256), (256, 256)]
+STEPS = 6
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _build(device):
+    torch.manual_seed(5)
+    model = torch.nn.Module()
+    model.layers = torch.nn.ModuleList()
+    for rows, cols in SHAPES:
+        blk = torch.nn.Module()
+        blk.up_proj = torch.nn.Linear(cols, rows, bias=False)
+        model.layers.append(blk)
+    return model.to(device=device, dtype=torch.bfloat16)
+
+
+def _run(model, process_group=None) -> dict[str, torch.Tensor]:
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    opt = MuZOClipOptimizer(model, seed=21, horizon=4, min_history=2, process_group=process_group)
+    w0 = model.layers[0].up_proj.weight
+
+    def closure():
+        return float(w0.float().square().sum().item())
+
+    for _ in range(STEPS):
+        opt.estimate_projection(closure)
+        opt.step()
+    torch.cuda.synchronize()
+    return {n: p.detach().cpu() for n, p in model.named_parameters()}
+
+
+def _worker(rank: int, world: int, port: int, out_prefix: str) -> None:
+    sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        weights = _run(_build(torch.device("cuda", rank)), dist.group.WORLD)
+        torch.save(weights, f"{out_prefix}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_match_one_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ref = _run(_build(torch.device("cuda", 0)))
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path / "w")), nprocs=2, start_method="spawn",
+                       join=True)
+    moved = sum(int(not torch.equal(ref[n], v)) for n, v in _build(torch.device("cpu")).named_parameters())
+    assert moved == len(SHAPES)  # every selected matrix was updated
+    for r in range(2):
+        got = torch.load(tmp_path / f"w.{r}")
+        for name, value in ref.items():
+            assert torch.equal(value, got[name]), (r, name)
