@@ -4,8 +4,9 @@
 // make_zo_noise_like (muzo_clip/prng.py:39-81): a fresh Philox4x32-10 generator keyed by
 // hash64(step seed, name, shape, block), drawn by a grid-stride launch in which thread t of S
 // fills elements t + S*(4c + j) from the j-th word of its c-th Philox block. The kernels here
-// regenerate exactly those words with cuRAND's Philox device API (curand_init/curand4/
-// curand_normal4 called, not re-implemented) but organise the work for HBM: one work item is 8
+// regenerate exactly those words (Philox4x32-10 below, from its publication) and, for normal
+// noise, pass them through cuRAND's own Box-Muller transform (_curand_box_muller, called, not
+// re-implemented), but organise the work for HBM: one work item is 8
 // consecutive threads t..t+7 of one loop trip c, i.e. four 16-byte vectors (j = 0..3) of 8
 // consecutive elements. Warps therefore read and write contiguous 512-byte runs, and the noise
 // never touches memory.
@@ -40,18 +41,25 @@ __device__ __forceinline__ uint4 thread_words(uint64_t key, uint64_t t, uint64_t
                        static_cast<uint32_t>(key), static_cast<uint32_t>(key >> 32));
 }
 
+// curand_normal4 of a Philox state positioned at the block `thread_words` returns: cuRAND's own
+// Box-Muller transform (_curand_box_muller, called, not restated) on the four words, without
+// the state set-up of curand_init.
+__device__ __forceinline__ float4 normal4_from_words(uint4 r) {
+  const float2 a = _curand_box_muller(r.x, r.y);
+  const float2 b = _curand_box_muller(r.z, r.w);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // Noise of 8 consecutive launch threads t0..t0+7 for loop trip `trip`: z[j][k] is element
 // t0 + k + S*(4*trip + j). `word_offset` is the launch's Philox offset (32-bit words). Normal
-// noise calls cuRAND's Box-Muller transform on the same Philox stream (curand_normal4).
+// noise applies cuRAND's Box-Muller transform to the same Philox words (curand_normal4).
 template <int DIST>
 __device__ __forceinline__ void noise8x4(uint64_t key, uint64_t t0, uint64_t word_offset,
                                          uint64_t trip, float (&z)[4][8]) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     if (DIST == MUZO_NORMAL) {
-      curandStatePhilox4_32_10_t st;
-      curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
-      float4 n = curand_normal4(&st);
+      const float4 n = normal4_from_words(thread_words(key, t0 + k, word_offset, trip));
       // randn's transform is rand * std + mean with std = 1, mean = 0
       z[0][k] = n.x; z[1][k] = n.y; z[2][k] = n.z; z[3][k] = n.w;
     } else {
@@ -279,9 +287,7 @@ __device__ __forceinline__ void accumulate4x4(uint64_t key, uint64_t t0, uint64_
   for (int k = 0; k < 4; ++k) {
     if (DIST == MUZO_NORMAL && k > 0) asm volatile("" ::: "memory");
     if (DIST == MUZO_NORMAL) {
-      curandStatePhilox4_32_10_t st;
-      curand_init(key, t0 + k, word_offset + 4ull * trip, &st);
-      float4 n = curand_normal4(&st);
+      float4 n = normal4_from_words(thread_words(key, t0 + k, word_offset, trip));
       round2_to(n.x, n.y, PDTYPE);
       round2_to(n.z, n.w, PDTYPE);
       acc[0][k] = __fmaf_rn(alpha, n.x, acc[0][k]);

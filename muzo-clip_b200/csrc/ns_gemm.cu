@@ -68,6 +68,7 @@ struct GemmArgs {
   const __nv_bfloat16* e;
   float c1, c2;
   int32_t* status;
+  int32_t* sched;          // CTA-pair kernel: [0] next tile, [1] pairs finished (zero between launches)
 };
 
 template <int EPI>
@@ -356,6 +357,8 @@ constexpr int PA_BYTES = PHALF * BK * 2;   // 16 KB
 constexpr int PB_BYTES = PHALF * BK * 2;   // 16 KB
 constexpr int P_STAGE_BYTES = PA_BYTES + PB_BYTES;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int TILE_SLOTS = 4;   // tile-index ring from the leader's producer to every other role
+constexpr int TILE_READERS = 10;  // leader MMA + 4 epilogue warps per CTA + the peer's producer
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -419,6 +422,31 @@ __device__ __forceinline__ void pair_abort(int* flag) {
     asm volatile("st.release.cluster.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(a, r)), "r"(1) : "memory");
 }
 
+// Tile ring: the leader's producer takes tile indices from a global counter (atomicAdd), so a
+// pair that starts late or runs slower — SMs held by a concurrent kernel such as an NCCL
+// transfer — simply takes fewer tiles. Slot k % TILE_SLOTS of both CTAs receives the index of the
+// pair's k-th tile (-1 when the counter passed the last tile); every other role reads it there
+// and releases the slot on the leader.
+__device__ __forceinline__ void publish_tile(int* slot, uint64_t* full, int t) {
+#pragma unroll
+  for (uint32_t r = 0; r < 2; ++r) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(smem_u32(slot), r)), "r"(t) : "memory");
+    mbar_arrive_cluster(map_to_rank(smem_u32(full), r));
+  }
+}
+
+// Wait for the pair's k-th tile index; false when the wait expired.
+__device__ __forceinline__ bool read_tile(const int* slots, uint64_t* full, int64_t k, int& t) {
+  const int s = static_cast<int>(k % TILE_SLOTS);
+  if (!mbar_wait_cluster(full + s, static_cast<uint32_t>((k / TILE_SLOTS) & 1))) return false;
+  t = *reinterpret_cast<const volatile int*>(slots + s);
+  return true;
+}
+
+__device__ __forceinline__ void release_tile(uint64_t* empty, int64_t k) {
+  mbar_arrive_cluster(map_to_rank(smem_u32(empty + k % TILE_SLOTS), 0));
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -431,19 +459,22 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   uint64_t* tfull = empty + P_STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tile_full = drain + 1;
+  uint64_t* tile_empty = tile_full + TILE_SLOTS;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tile_empty + TILE_SLOTS);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
+  int* tile_slots = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
-  const int64_t pair = blockIdx.x >> 1;
   const int64_t npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 8); }
+    for (int s = 0; s < TILE_SLOTS; ++s) { mbar_init(tile_full + s, 1); mbar_init(tile_empty + s, TILE_READERS); }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -468,7 +499,21 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       uint32_t phase = 0;
       bool ok = true;
       uint32_t armed = 0, armed_parity = 0;  // leader: stages armed, and their last parity
-      for (int64_t t = pair; t < g.num_tiles && ok; t += npairs) {
+      for (int64_t k = 0; ok; ++k) {
+        int t = -1;
+        if (leader) {
+          if (!mbar_wait(tile_empty + k % TILE_SLOTS, static_cast<uint32_t>(((k / TILE_SLOTS) & 1) ^ 1))) {
+            ok = false;
+            break;
+          }
+          t = atomicAdd(g.sched, 1);
+          if (t >= g.num_tiles) t = -1;
+          publish_tile(tile_slots + k % TILE_SLOTS, tile_full + k % TILE_SLOTS, t);
+        } else {
+          if (!read_tile(tile_slots, tile_full, k, t)) { ok = false; break; }
+          release_tile(tile_empty, k);
+        }
+        if (t < 0) break;
         int64_t b; int tm, tn;
         tile_coords(g, t, b, tm, tn);
         const int m0 = tm * PM + static_cast<int>(rank) * PHALF;
@@ -515,8 +560,11 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int64_t local = 0;
-      for (int64_t t = pair; t < g.num_tiles && ok; t += npairs, ++local) {
+      for (int64_t local = 0; ok; ++local) {
+        int t = -1;
+        if (!read_tile(tile_slots, tile_full, local, t)) { ok = false; break; }
+        release_tile(tile_empty, local);
+        if (t < 0) break;
         const int acc = static_cast<int>(local & 1);
         const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
         if (!mbar_wait(tempty + acc, acc_phase ^ 1)) { ok = false; break; }
@@ -545,9 +593,18 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int lane_base = 32 * (warp & 3);
     const uint32_t leader_tempty0 = map_to_rank(smem_u32(tempty), 0);
-    int64_t local = 0;
     bool ok = true;
-    for (int64_t t = pair; t < g.num_tiles; t += npairs, ++local) {
+    for (int64_t local = 0;; ++local) {
+      int t = -1;
+      bool got = true;
+      if (lane == 0) {
+        got = read_tile(tile_slots, tile_full, local, t);
+        if (got) release_tile(tile_empty, local);
+      }
+      got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+      t = __shfl_sync(0xffffffffu, t, 0);
+      if (!got) { ok = false; break; }
+      if (t < 0) break;
       int64_t b; int tm, tn;
       tile_coords(g, t, b, tm, tn);
       const int acc = static_cast<int>(local & 1);
@@ -584,6 +641,15 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+  if (leader && threadIdx.x == 0) {
+    // the last pair to finish (every pair has taken its final index by now) rewinds the counter
+    // for the next launch that uses this status buffer
+    __threadfence();
+    if (atomicAdd(g.sched + 1, 1) == static_cast<int>(npairs) - 1) {
+      atomicExch(g.sched, 0);
+      atomicExch(g.sched + 1, 0);
+    }
   }
 }
 
@@ -671,7 +737,7 @@ bool use_pair_kernel(int64_t m, int64_t n) {
   return m >= PM && n >= PN;
 }
 
-__device__ int32_t g_default_status;
+__device__ int32_t g_default_status[4];
 
 bool aligned16h(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -741,7 +807,9 @@ int muzo_ns_gemm(const void* a, int64_t lda, int64_t a_batch_stride, int a_mn, c
     MUZO_CUDA_CHECK(cudaGetSymbolAddress(&p, g_default_status));
     d_status = static_cast<int32_t*>(p);
   }
+  if (g.num_tiles >= (1ll << 30)) return MUZO_ERR_UNSUPPORTED;
   g.status = d_status;
+  g.sched = d_status + 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (epilogue) {
     case MUZO_EPI_STORE: return launch_epi<MUZO_EPI_STORE>(pair, a_mn, b_mn, ma, mb, g, s);

@@ -44,6 +44,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with acquire at cluster scope: for barriers that another CTA of the cluster arrives on
+// after writing data the waiter then reads.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait_cluster(addr, parity)) return true;
+  const long long start = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(addr, parity)) return true;
+    if (static_cast<unsigned long long>(clock64() - start) > kWaitLimitCycles) return false;
+  }
+}
+
 // Bounded wait for the phase with parity `parity` to complete. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);

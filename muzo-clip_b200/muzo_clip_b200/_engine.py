@@ -221,7 +221,8 @@ class StepEngine:
         first_seen: dict[tuple[int, int, int], int] = {}
         for b in self.blocks:
             first_seen.setdefault((b.rows, b.cols, _lib.dtype_code(b.dtype)), len(first_seen))
-        self.class_order = sorted(first_seen, key=lambda ck: (ck[0] * ck[1], first_seen[ck]))
+        desc = os.environ.get("MUZO_COLLECTIVES", "end") == "class"
+        self.class_order = sorted(first_seen, key=lambda ck: ((-1 if desc else 1) * ck[0] * ck[1], first_seen[ck]))
         owned_by_class: dict[tuple[int, int, int], list[Block]] = {ck: [] for ck in self.class_order}
         for b in self.owned:
             owned_by_class[(b.rows, b.cols, _lib.dtype_code(b.dtype))].append(b)

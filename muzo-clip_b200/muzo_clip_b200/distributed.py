@@ -11,6 +11,8 @@ the next use of the weights. Per-block statistics are combined with one small al
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 import torch.distributed as dist
@@ -25,16 +27,32 @@ class ShardedStepEngine(StepEngine):
         world = dist.get_world_size(process_group)
         super().__init__(opt, rank=rank, world=world, process_group=process_group)
         self._pending: list = []
+        self._handles: list = []
         self._global_ranks = [dist.get_global_rank(process_group, r) if process_group is not None else r
                               for r in range(world)] if process_group is not None else list(range(world))
 
     def _after_class(self, class_key) -> None:
-        """Record that the blocks of `class_key` are final on their owners. The transfers start in
-        `_finish_collectives`, after the last GEMM: NCCL kernels running next to the persistent
-        Newton-Schulz GEMMs hold SMs that the GEMMs' statically scheduled CTAs then wait for
-        (measured on 2 B200s: 378 ms per step with per-class overlap, 361 ms deferred)."""
-        if self.world > 1:
+        """The blocks of `class_key` are final on their owners (their GEMMs are queued)."""
+        if self.world <= 1:
+            return
+        if os.environ.get("MUZO_COLLECTIVES", "end") == "class":
+            self._handles.append(self._broadcast(self._class_blocks([class_key])))
+        else:
             self._pending.append(class_key)
+
+    def _class_blocks(self, class_keys) -> list:
+        return [b for ck in class_keys for b in self.blocks if (b.rows, b.cols, self._code(b)) == ck]
+
+    def _broadcast(self, blocks):
+        """Broadcast `blocks` from their owners in one NCCL group (async)."""
+        manager = getattr(dist, "_coalescing_manager", None)
+        if dist.get_backend(self.group) == "nccl" and manager is not None:
+            with manager(group=self.group, device=self.device, async_ops=True) as cm:
+                for b in blocks:
+                    dist.broadcast(b.tensor, src=self._global_ranks[self.owner[b.index]], group=self.group)
+            return cm
+        return [dist.broadcast(b.tensor, src=self._global_ranks[self.owner[b.index]], group=self.group,
+                               async_op=True) for b in blocks]
 
     @staticmethod
     def _code(b) -> int:
@@ -43,24 +61,14 @@ class ShardedStepEngine(StepEngine):
         return _lib.dtype_code(b.dtype)
 
     def _finish_collectives(self) -> None:
-        """Broadcast every owned block from its owner, all classes in one NCCL group (the ranks
-        take the same classes in the same order), and make the current stream wait for them."""
+        """Issue what is still pending and make the current stream wait for every transfer."""
         pending, self._pending = self._pending, []
-        if not pending:
-            return
-        todo = [b for ck in pending for b in self.blocks if (b.rows, b.cols, self._code(b)) == ck]
-        backend = dist.get_backend(self.group)
-        manager = getattr(dist, "_coalescing_manager", None)
-        if backend == "nccl" and manager is not None:
-            with manager(group=self.group, device=self.device, async_ops=True) as cm:
-                for b in todo:
-                    dist.broadcast(b.tensor, src=self._global_ranks[self.owner[b.index]], group=self.group)
-            cm.wait()
-            return
-        works = [dist.broadcast(b.tensor, src=self._global_ranks[self.owner[b.index]], group=self.group,
-                                async_op=True) for b in todo]
-        for w in works:
-            w.wait()
+        if pending:
+            self._handles.append(self._broadcast(self._class_blocks(pending)))
+        handles, self._handles = self._handles, []
+        for h in handles:
+            for w in (h if isinstance(h, list) else [h]):
+                w.wait()
 
     def gather_stats(self, per_block: dict[int, dict]) -> dict[int, dict]:
         """Combine the owners' per-block statistics on every rank (sum all-reduce)."""

@@ -46,12 +46,14 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         class Fake:  # the collective parts of ShardedStepEngine on CPU tensors
             _after_class = ShardedStepEngine._after_class
             _finish_collectives = ShardedStepEngine._finish_collectives
+            _class_blocks = ShardedStepEngine._class_blocks
+            _broadcast = ShardedStepEngine._broadcast
             gather_stats = ShardedStepEngine.gather_stats
             _code = staticmethod(ShardedStepEngine._code)
 
         eng = Fake()
         eng.blocks, eng.owner, eng.world, eng.group = blocks, owner, world, dist.group.WORLD
-        eng._pending, eng._global_ranks, eng.device = [], list(range(world)), torch.device("cpu")
+        eng._pending, eng._handles, eng._global_ranks, eng.device = [], [], list(range(world)), torch.device("cpu")
         # owners "update" their blocks; everyone else holds stale values
         for b in blocks:
             if owner[b.index] == rank:

@@ -162,14 +162,14 @@ def _gemm_case(device, m, n, k, batch, a_mn, b_mn, epi):
     B_st = padded(B_log if b_mn else B_log.transpose(1, 2))   # [k][n] or [n][k]
     E = padded(rnd(batch, m, n))
     D = torch.zeros_like(E)
-    status = torch.zeros(1, dtype=torch.int32, device=device)
+    status = torch.zeros(4, dtype=torch.int32, device=device)  # status + scheduler words
     c1, c2 = np.float32(-4.775), np.float32(2.0315)
     lda, ldb, ldd = A_st.shape[-1], B_st.shape[-1], D.shape[-1]
     L.check(L.lib.muzo_ns_gemm(A_st.data_ptr(), lda, A_st[0].numel(), a_mn, B_st.data_ptr(), ldb, B_st[0].numel(), b_mn,
                                D.data_ptr(), ldd, D[0].numel(), E.data_ptr() if epi else None, epi, float(c1),
                                float(c2), m, n, k, batch, 0, status.data_ptr(), L.stream_ptr(device)), "gemm")
     torch.cuda.synchronize()
-    assert int(status.item()) == 0
+    assert status.tolist() == [0, 0, 0, 0]  # no wait expired; scheduler counters rewound
     acc = torch.matmul(A_log.float(), B_log.float())
     D = D[..., :n]
     E = E[..., :n]
@@ -232,7 +232,7 @@ def test_ns_gemm_symmetric_outputs(device, gemm_kernel, m, k, batch, tall):
         X = torch.zeros((batch, m, ldk), dtype=torch.bfloat16, device=device)
         X[..., :k] = torch.randn((batch, m, k), generator=g).to(torch.bfloat16).to(device)
         a_args = (X.data_ptr(), ldk, m * ldk, 0, X.data_ptr(), ldk, m * ldk, 0)
-    status = torch.zeros(1, dtype=torch.int32, device=device)
+    status = torch.zeros(4, dtype=torch.int32, device=device)  # status + scheduler words
     outs = {}
     for sym in (0, 1):
         A = torch.zeros((batch, m, ld), dtype=torch.bfloat16, device=device)
@@ -244,7 +244,7 @@ def test_ns_gemm_symmetric_outputs(device, gemm_kernel, m, k, batch, tall):
                                    status.data_ptr(), L.stream_ptr(device)), "poly")
         torch.cuda.synchronize()
         outs[sym] = (A[..., :m].float().cpu(), B[..., :m].float().cpu())
-    assert int(status.item()) == 0
+    assert status.tolist() == [0, 0, 0, 0]  # no wait expired; scheduler counters rewound
     upper = torch.triu(torch.ones((m, m), dtype=torch.bool))
     A0, B0 = outs[0]
     A1, B1 = outs[1]
