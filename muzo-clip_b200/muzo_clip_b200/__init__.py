@@ -8,11 +8,13 @@ from .muzo_optimizer import MuZOClipOptimizer
 from .newton_schulz import zeropower_via_newtonschulz5
 from .parameter_filter import select_muzo_parameters
 from .prng import iter_param_blocks, make_zo_noise_like
+from .qk_clip import use_qk_capture_attention
 
 __all__ = [
     "MuZOClipOptimizer",
     "iter_param_blocks",
     "make_zo_noise_like",
     "select_muzo_parameters",
+    "use_qk_capture_attention",
     "zeropower_via_newtonschulz5",
 ]

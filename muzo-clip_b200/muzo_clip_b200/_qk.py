@@ -54,6 +54,18 @@ def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: 
 
         group = query.shape[1] // key.shape[1]
         kr = key.repeat_interleave(group, dim=1)
+        if attention_mask.dtype == torch.bool:  # SDPA's boolean form -> eager's additive form
+            keep = attention_mask
+            if causal:
+                # transformers un-masks rows that would be fully masked (padding queries) so that
+                # SDPA returns no NaN; eager attention keeps them masked: in a causal model such
+                # a row is the one that sees a key above the diagonal
+                sq_, sk_ = keep.shape[-2], keep.shape[-1]
+                i = torch.arange(sq_, device=keep.device)[:, None] + (sk_ - sq_)
+                above = torch.arange(sk_, device=keep.device)[None, :] > i
+                keep = keep & ~(keep & above).any(dim=-1, keepdim=True)
+            attention_mask = torch.zeros(keep.shape, dtype=query.dtype, device=query.device).masked_fill(
+                ~keep, torch.finfo(query.dtype).min)
         logits = torch.matmul(query, kr.transpose(2, 3)) * scaling + attention_mask
         return logits_head_max(logits)
     q, k = query, key
@@ -73,15 +85,16 @@ def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: 
 
 
 def _is_plain_causal(mask: torch.Tensor, sq: int, sk: int) -> bool:
-    """True when an additive [B|1, 1|H, Sq, Sk] mask is 0 on and below the (end-aligned)
-    diagonal and a large negative value above it for every batch row."""
-    if mask.dtype == torch.bool:
-        return False
+    """True when a [B|1, 1|H, Sq, Sk] mask is the plain causal mask for every batch row: an
+    additive mask 0 on and below the (end-aligned) diagonal and a large negative value above
+    it, or a boolean mask True exactly on and below it."""
     if mask.ndim != 4 or mask.shape[-2] != sq or mask.shape[-1] != sk:
         return False
     i = torch.arange(sq, device=mask.device)[:, None] + (sk - sq)
     j = torch.arange(sk, device=mask.device)[None, :]
     upper = j > i
+    if mask.dtype == torch.bool:
+        return bool((mask == ~upper).all())
     m = mask.float()
     lower_ok = bool((m[..., ~upper] == 0).all())
     upper_ok = bool((m[..., upper] <= torch.finfo(torch.bfloat16).min / 2).all()) if upper.any() else True
@@ -134,17 +147,22 @@ def scale_rows(weight: torch.Tensor, groups: int, rows_per_group: int, factors: 
 
 
 def _probe_attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
-    """Attention function used during a probe forward: records the per-head max logit with the
-    kernel, then returns SDPA's output."""
+    """Attention function of the probe and of training-time capture: SDPA computes the output
+    (and its backward); while a QK-Clip capture is active, the library's max-logit kernel reads
+    the same post-RoPE query and key states and records the per-head max of the pre-softmax
+    logits. Outside a capture it is SDPA alone."""
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
 
     ctrl = _ACTIVE.get()
     if scaling is None:
         scaling = query.shape[-1] ** -0.5
     if ctrl is not None:
-        causal = bool(getattr(module, "is_causal", True)) and query.shape[2] > 1
-        mask = attention_mask if attention_mask is not None and attention_mask.ndim == 4 else None
-        ctrl.record_qk(module, query, key, float(scaling), causal if mask is None else True, mask)
+        with torch.no_grad():
+            sq = query.shape[2]
+            mask = attention_mask if attention_mask is not None and attention_mask.ndim == 4 else None
+            # no mask: SDPA runs causal when the module is causal and there is more than one query
+            causal = True if mask is not None else bool(getattr(module, "is_causal", True)) and sq > 1
+            ctrl.record_qk(module, query.detach(), key.detach(), float(scaling), causal, mask)
     return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
                                   **kwargs)
 
@@ -162,3 +180,22 @@ def ensure_probe_registered() -> str:
         ALL_MASK_ATTENTION_FUNCTIONS.register(PROBE_ATTENTION, eager_mask)
         _REGISTERED = True
     return PROBE_ATTENTION
+
+
+_TRAINING_REGISTERED = False
+
+
+def ensure_training_registered() -> str:
+    """Register the training-time capture attention with SDPA's mask format (no mask for plain
+    causal attention, so SDPA keeps its fused causal kernels) once."""
+    global _TRAINING_REGISTERED
+    from .qk_clip import CAPTURE_ATTENTION
+
+    if not _TRAINING_REGISTERED:
+        from transformers import AttentionInterface
+        from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS, sdpa_mask
+
+        AttentionInterface.register(CAPTURE_ATTENTION, _probe_attention)
+        ALL_MASK_ATTENTION_FUNCTIONS.register(CAPTURE_ATTENTION, sdpa_mask)
+        _TRAINING_REGISTERED = True
+    return CAPTURE_ATTENTION

@@ -31,6 +31,28 @@ from . import _qk
 logger = logging.getLogger(__name__)
 
 PROBE_ATTENTION = "muzo_qk_probe"
+CAPTURE_ATTENTION = "muzo_qk_sdpa"
+
+
+def use_qk_capture_attention(model: torch.nn.Module) -> str:
+    """Make ``model`` (a transformers model) train with the QK-capture attention: SDPA for the
+    output and gradients, plus the library's max-logit kernel on the same query/key states
+    while a QK-Clip capture is active — e.g. the clean forward of
+    ``MuZOClipOptimizer(..., enable_qk_clip=True, qk_capture_clean_forward=True)`` — so exact
+    per-head maxima are collected without eager attention and without a separate probe. Outside
+    a capture the attention is SDPA alone. Returns the implementation name."""
+    impl = _qk.ensure_training_registered()
+    seen: list[Any] = []
+    for module in model.modules():
+        config = getattr(module, "config", None)
+        if config is None or any(config is c for c in seen):
+            continue
+        seen.append(config)
+        if hasattr(config, "_attn_implementation"):
+            config._attn_implementation = impl
+    if not seen:
+        raise ValueError("use_qk_capture_attention expects a transformers model (no config found)")
+    return impl
 
 
 @dataclass

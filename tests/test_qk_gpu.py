@@ -167,3 +167,77 @@ def test_probe_reports_disabled_without_modules(device):
     opt = MuZOClipOptimizer(model, enable_qk_clip=True)
     st = opt.probe_and_apply_qk_clip(lambda: torch.tensor(1.0))
     assert st["enabled"] is False and st["disabled_reason"] == "no q_proj/k_proj attention modules found"
+
+
+@pytest.mark.parametrize("padded", [False, True])
+def test_training_capture_attention(device, padded):
+    """use_qk_capture_attention: outputs and gradients are SDPA's; the clean forward of
+    estimate_projection (qk_capture_clean_forward=True) records the eager maxima exactly, with
+    and without a padding mask; apply_qk_clip_if_available then clips."""
+    from muzo_clip_b200 import MuZOClipOptimizer, use_qk_capture_attention
+
+    model = _tiny_llama(torch.bfloat16, device)
+    with torch.no_grad():
+        model.model.layers[0].self_attn.q_proj.weight.mul_(40.0)
+    sdpa = copy.deepcopy(model)
+    ids = torch.randint(0, 1024, (3, 48), generator=torch.Generator().manual_seed(2)).to(device)
+    mask = torch.ones_like(ids)
+    if padded:
+        mask[1, :7] = 0  # left padding of one row
+    assert use_qk_capture_attention(model) == "muzo_qk_sdpa"
+
+    # no capture active: the same function as SDPA, forward and backward
+    model.train(), sdpa.train()
+    out = model(input_ids=ids, attention_mask=mask, labels=ids)
+    ref = sdpa(input_ids=ids, attention_mask=mask, labels=ids)
+    assert torch.equal(out.logits, ref.logits)
+    out.loss.backward()
+    ref.loss.backward()
+    g1 = model.model.layers[0].self_attn.q_proj.weight.grad
+    g2 = sdpa.model.layers[0].self_attn.q_proj.weight.grad
+    assert g1 is not None and torch.equal(g1, g2)
+    model.zero_grad(set_to_none=True)
+    model.eval()
+
+    twin = copy.deepcopy(sdpa)
+    opt = MuZOClipOptimizer(model, enable_qk_clip=True, qk_capture_clean_forward=True, qk_clip_tau=5.0,
+                            restore_exact=True, seed=3)
+
+    def closure():
+        with torch.no_grad():
+            return model(input_ids=ids, attention_mask=mask, labels=ids).loss
+
+    proj = opt.estimate_projection(closure)
+    assert not proj["skipped"]
+    captured = {k: v.cpu() for k, v in opt.qk_clip._captured_smax.items()}
+    # reference: eager softmax inputs of the same (restored, clean) weights
+    names = {id(m): n for n, m in twin.named_modules() if hasattr(m, "q_proj") and hasattr(m, "k_proj")}
+    stack, want, hooks = [], {}, []
+    for mod_id, name in names.items():
+        mod = next(m for m in twin.modules() if id(m) == mod_id)
+        hooks.append(mod.register_forward_pre_hook(lambda m, a, name=name: stack.append(name)))
+        hooks.append(mod.register_forward_hook(lambda m, a, o: stack.pop() and None))
+    import torch.nn.functional as F
+    orig = F.softmax
+
+    def patched(inp, *args, **kwargs):
+        if stack and inp.ndim == 4:
+            per = inp.detach().float().amax(dim=(0, 2, 3)).cpu()
+            prev = want.get(stack[-1])
+            want[stack[-1]] = per if prev is None else torch.maximum(prev, per)
+        return orig(inp, *args, **kwargs)
+
+    twin.config._attn_implementation = "eager"
+    F.softmax = patched
+    try:
+        with torch.no_grad():
+            twin(input_ids=ids, attention_mask=mask)
+    finally:
+        F.softmax = orig
+        for h in hooks:
+            h.remove()
+    assert set(captured) == set(want)
+    for name, ref_max in want.items():
+        assert bool(((captured[name] - ref_max).abs() <= _ulp(ref_max, 7)).all()), (name, captured[name], ref_max)
+    stats = opt.qk_clip.apply()  # the clip that apply_qk_clip_if_available runs after an updating step
+    assert stats.enabled and stats.exact_logits and stats.qk_clip_count > 0
