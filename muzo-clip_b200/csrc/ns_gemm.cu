@@ -360,68 +360,6 @@ constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr int TILE_SLOTS = 4;   // tile-index ring from the leader's producer to every other role
 constexpr int TILE_READERS = 10;  // leader MMA + 4 epilogue warps per CTA + the peer's producer
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
-  return out;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx_u32(uint32_t saddr, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr), "r"(bytes) : "memory");
-}
-
-// 3-D TMA load into this CTA's shared memory whose completion is counted on the mbarrier at
-// cluster address `bar` (the leader CTA's stage barrier).
-__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t bar, void* dst, int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive on the barrier at the same shared-memory offset in both CTAs of the pair once the MMAs
-// issued so far have completed.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-// Raise the abort flag in both CTAs of the pair (same shared-memory offset in each).
-__device__ __forceinline__ void pair_abort(int* flag) {
-  const uint32_t a = smem_u32(flag);
-#pragma unroll
-  for (uint32_t r = 0; r < 2; ++r)
-    asm volatile("st.release.cluster.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(a, r)), "r"(1) : "memory");
-}
-
 // Tile ring: the leader's producer takes tile indices from a global counter (atomicAdd), so a
 // pair that starts late or runs slower — SMs held by a concurrent kernel such as an NCCL
 // transfer — simply takes fewer tiles. Slot k % TILE_SLOTS of both CTAs receives the index of the

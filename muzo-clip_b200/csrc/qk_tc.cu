@@ -11,6 +11,8 @@
 // Layout of the kernel follows the Newton-Schulz GEMM: persistent CTAs (one per SM), warp 0 TMA
 // producer into a 4-stage ring, warp 1 TMEM owner and MMA issuer with two 256-column
 // accumulators, warps 2-5 epilogue; every wait is bounded.
+#include <cstdlib>
+
 #include "tcgen05_common.cuh"
 
 namespace muzo {
@@ -238,6 +240,325 @@ qk_max_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair kernel
+// A 2-CTA cluster takes a contiguous range of (batch*head, 256-query block, 256-key block) tiles.
+// Each CTA keeps its 128 query rows of the current query block resident in shared memory
+// (two buffers, so the next block loads while the current one computes) and streams its 128
+// keys of each key block: per SM
+// 16 KB of K per 64-deep slice for a 256 x 256 MMA tile (tcgen05.mma.cta_group::2, M = N = 256).
+// Eight epilogue warps per CTA (two per TMEM lane quarter, 128 columns each) fold the tile into
+// per-thread running max / min registers with NaN-propagating max, and flush them with one
+// atomicMax per warp when the head changes.
+constexpr int PQ_ROWS = 128;                         // queries per CTA; a pair covers 256
+constexpr int PK_ROWS = 128;                         // keys per CTA per tile; a pair tile covers 256
+constexpr int PQ_MAX_KB = 4;                         // head dim up to 256 = 4 slices of 64
+constexpr int PQ_SUB_BYTES = PQ_ROWS * QBK * 2;      // 16 KB per slice
+constexpr int PK_STAGE_BYTES = PK_ROWS * QBK * 2;    // 16 KB
+constexpr int PK_MAX_STAGES = 12;
+constexpr int PQ_SLOTS = 2;                          // query-block buffers
+constexpr int PQK_TILE_BYTES = 192 * 1024;           // query buffers + key stages
+constexpr int PQK_THREADS = 320;                     // warp 0 TMA, warp 1 TMEM + MMA, warps 2..9 epilogue
+constexpr int PQK_EPI_WARPS = 8;
+constexpr int PQK_SMEM_BYTES = PQK_TILE_BYTES + 1024 + 512;
+
+struct QkPairArgs {
+  int64_t sq, sk, shift;
+  int hq, group, nqb, causal, num_kb;
+  int k_stages;            // key stages in the shared memory the query buffers leave
+  int64_t tiles_per_bh, num_tiles;
+  int* enc;
+  int32_t* valid;
+  int32_t* status;
+};
+
+__device__ __forceinline__ int pair_kv_tiles(const QkPairArgs& g, int qb) {
+  int64_t end = g.sk;
+  if (g.causal) {
+    const int64_t last = static_cast<int64_t>(qb + 1) * 2 * PQ_ROWS + g.shift;  // keys visible to the block's last row
+    end = last < g.sk ? last : g.sk;
+    if (end < 0) end = 0;
+  }
+  return static_cast<int>((end + 2 * PK_ROWS - 1) / (2 * PK_ROWS));
+}
+
+// flat tile -> (batch*head, query block, key block)
+__device__ __forceinline__ void pair_qk_tile(const QkPairArgs& g, int64_t t, int64_t& bh, int& qb, int& kv) {
+  bh = t / g.tiles_per_bh;
+  int64_t r = t - bh * g.tiles_per_bh;
+  int q = 0;
+  while (q < g.nqb) {
+    const int w = pair_kv_tiles(g, q);
+    if (r < w) break;
+    r -= w;
+    ++q;
+  }
+  qb = q;
+  kv = static_cast<int>(r);
+}
+
+// Sequential walk over a contiguous tile range: decoded once, then advanced without divisions
+// (a 64-bit division per tile on every role's critical path costs more than the tile's MMAs).
+struct PairTileCursor {
+  int64_t bh;
+  int qb, kv, nkv;
+  __device__ __forceinline__ void start(const QkPairArgs& g, int64_t t) {
+    pair_qk_tile(g, t, bh, qb, kv);
+    nkv = pair_kv_tiles(g, qb);
+  }
+  // true when the next tile starts a new query block
+  __device__ __forceinline__ bool last_of_block() const { return kv + 1 >= nkv; }
+  __device__ __forceinline__ void advance(const QkPairArgs& g) {
+    if (++kv < nkv) return;
+    kv = 0;
+    do {  // query blocks without visible keys hold no tiles
+      if (++qb == g.nqb) { qb = 0; ++bh; }
+      nkv = pair_kv_tiles(g, qb);
+    } while (nkv == 0);
+  }
+};
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+template <int FMT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PQK_THREADS, 1)
+qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                   QkPairArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const int PQ_SLOT_BYTES = g.num_kb * PQ_SUB_BYTES;
+  const int PK_STAGES = g.k_stages;
+  uint8_t* sq_slots = smem;                                        // [PQ_SLOTS][num_kb][128 x 64]
+  uint8_t* sk_stages = smem + PQ_SLOTS * PQ_SLOT_BYTES;            // [k_stages][128 x 64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PQK_TILE_BYTES);
+  uint64_t* empty = full + PK_MAX_STAGES;
+  uint64_t* tfull = empty + PK_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* q_full = tempty + 2;
+  uint64_t* q_empty = q_full + PQ_SLOTS;
+  uint64_t* drain = q_empty + PQ_SLOTS;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int64_t t_begin = pair * g.num_tiles / npairs, t_end = (pair + 1) * g.num_tiles / npairs;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PK_STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 2 * PQK_EPI_WARPS); }
+    for (int q = 0; q < PQ_SLOTS; ++q) { mbar_init(q_full + q, 1); mbar_init(q_empty + q, 1); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(Q_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t armed = 0, armed_parity = 0;   // leader: K stages armed and their last parity
+      int64_t useq = -1;                      // sequence number of the current query block
+      PairTileCursor cur;
+      cur.start(g, t_begin);
+      int64_t cur_bh = -1;
+      int b = 0, h = 0;
+      for (int64_t t = t_begin; t < t_end && ok; ++t, cur.advance(g)) {
+        const int qb = cur.qb, kv = cur.kv;
+        if (cur.bh != cur_bh) {
+          cur_bh = cur.bh;
+          b = static_cast<int>(cur_bh / g.hq);
+          h = static_cast<int>(cur_bh - static_cast<int64_t>(b) * g.hq);
+        }
+        if (t == t_begin || kv == 0) {         // a new query block
+          ++useq;
+          // the MMAs of the block that used this buffer two blocks ago must be done with it
+          const int qs = static_cast<int>(useq % PQ_SLOTS);
+          if (!mbar_wait(q_empty + qs, static_cast<uint32_t>(((useq / PQ_SLOTS) & 1) ^ 1))) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx_u32(smem_u32(q_full + qs), 2u * g.num_kb * PQ_SUB_BYTES);
+          const uint32_t qbar = map_to_rank(smem_u32(q_full + qs), 0);
+          for (int kb = 0; kb < g.num_kb; ++kb)
+            tma_load_4d_pair(&map_q, qbar, sq_slots + qs * PQ_SLOT_BYTES + kb * PQ_SUB_BYTES, kb * QBK,
+                             qb * 2 * PQ_ROWS + static_cast<int>(rank) * PQ_ROWS, h, b);
+        }
+        const int kvh = h / g.group;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1)) { ok = false; break; }
+          if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
+          if (leader) {
+            mbar_arrive_expect_tx_u32(smem_u32(full + stage), 2u * PK_STAGE_BYTES);
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          }
+          tma_load_4d_pair(&map_k, map_to_rank(smem_u32(full + stage), 0), sk_stages + stage * PK_STAGE_BYTES,
+                           kb * QBK, kv * 2 * PK_ROWS + static_cast<int>(rank) * PK_ROWS, kvh, b);
+          if (++stage == PK_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) { atomicCAS(g.status, kErrNone, kErrTimeoutProducer); pair_abort(abort_flag); atomicExch(g.valid, 0); }
+      for (int s2 = 0; s2 < PK_STAGES; ++s2)
+        if (armed & (1u << s2)) mbar_wait(full + s2, (armed_parity >> s2) & 1u);
+      for (int64_t u = useq - (PQ_SLOTS - 1); leader && u <= useq; ++u)   // last load into each buffer
+        if (u >= 0) mbar_wait(q_full + u % PQ_SLOTS, static_cast<uint32_t>((u / PQ_SLOTS) & 1));
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_fmt(2 * PQ_ROWS, 2 * PK_ROWS, false, false, FMT);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int64_t useq = -1, local = 0;
+      PairTileCursor cur;
+      cur.start(g, t_begin);
+      for (int64_t t = t_begin; t < t_end && ok; ++t, ++local, cur.advance(g)) {
+        if (t == t_begin || cur.kv == 0) {     // a new query block
+          ++useq;
+          if (!mbar_wait(q_full + useq % PQ_SLOTS, static_cast<uint32_t>((useq / PQ_SLOTS) & 1))) { ok = false; break; }
+          tc_fence_after();
+        }
+        const int acc = static_cast<int>(local & 1);
+        if (!mbar_wait(tempty + acc, static_cast<uint32_t>(((local >> 1) & 1) ^ 1))) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * QN;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(full + stage, phase)) { ok = false; break; }
+          if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(sq_slots + (useq % PQ_SLOTS) * PQ_SLOT_BYTES + kb * PQ_SUB_BYTES);
+          const uint32_t sb = smem_u32(sk_stages + stage * PK_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < QBK / 16; ++k)
+            umma_f16_pair(tmem_d, make_sdesc(sa + k * 32, 16, 1024), make_sdesc(sb + k * 32, 16, 1024), idesc,
+                          (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(empty + stage);
+          if (++stage == PK_STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull + acc);
+        // the last tile of this query block in the range: Q may be replaced once its MMAs finish
+        if (t + 1 >= t_end || cur.last_of_block()) umma_commit_pair(q_empty + useq % PQ_SLOTS);
+      }
+      if (!ok) { atomicCAS(g.status, kErrNone, kErrTimeoutMma); pair_abort(abort_flag); atomicExch(g.valid, 0); }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..9, both CTAs)
+    const int quarter = warp & 3;                    // TMEM lanes this warp may access
+    const int colh = (warp - 2) >> 2;                // which 128 of the tile's 256 key columns
+    const uint32_t leader_tempty0 = map_to_rank(smem_u32(tempty), 0);
+    bool ok = true;
+    int64_t cur_bh = -1;
+    float best = -INFINITY, low = INFINITY;
+    auto flush = [&](int64_t bh) {
+      float m = best;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float l = low;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l = fminf(l, __shfl_xor_sync(0xffffffffu, l, o));
+      if (lane == 0) {
+        if (m != m || m == INFINITY || l == -INFINITY) atomicExch(g.valid, 0);
+        else if (m > -INFINITY) atomicMax(g.enc + static_cast<int>(bh % g.hq), encode_max(m));
+      }
+      best = -INFINITY;
+      low = INFINITY;
+    };
+    int64_t local = 0;
+    PairTileCursor cur;
+    cur.start(g, t_begin);
+    for (int64_t t = t_begin; t < t_end; ++t, ++local, cur.advance(g)) {
+      const int64_t bh = cur.bh;
+      const int qb = cur.qb, kv = cur.kv;
+      if (bh != cur_bh) {
+        if (cur_bh >= 0) flush(cur_bh);
+        cur_bh = bh;
+      }
+      const int acc = static_cast<int>(local & 1);
+      bool ready = true;
+      if (lane == 0) ready = mbar_wait(tfull + acc, static_cast<uint32_t>((local >> 1) & 1));
+      ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
+      if (!ready || *reinterpret_cast<volatile int*>(abort_flag)) { ok = ready; break; }
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(qb) * 2 * PQ_ROWS + static_cast<int64_t>(rank) * PQ_ROWS +
+                          32 * quarter + lane;
+      const int64_t jlim = g.causal ? row + g.shift : g.sk - 1;   // last visible key of this row
+      const int64_t jmax = jlim < g.sk - 1 ? jlim : g.sk - 1;
+      const int64_t j0 = static_cast<int64_t>(kv) * 2 * PK_ROWS + colh * 128;
+      uint32_t r[128];
+      tmem_ld128(tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) + acc * QN + colh * 128, r);
+      // the accumulator is in registers: hand it back to the MMA issuer before reducing it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
+      if (row < g.sq && j0 + 127 <= jmax) {
+        // eight independent max / min chains instead of one 128-long dependency chain
+        float m[8], n[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { m[e] = __uint_as_float(r[e]); n[e] = m[e]; }
+#pragma unroll
+        for (int e = 8; e < 128; ++e) {
+          const float x = __uint_as_float(r[e]);
+          m[e & 7] = max_nan(m[e & 7], x);
+          n[e & 7] = fminf(n[e & 7], x);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { best = max_nan(best, m[e]); low = fminf(low, n[e]); }
+      } else if (row < g.sq && j0 <= jmax) {
+#pragma unroll
+        for (int e = 0; e < 128; ++e) {
+          if (j0 + e <= jmax) {
+            const float x = __uint_as_float(r[e]);
+            best = max_nan(best, x);
+            low = fminf(low, x);
+          }
+        }
+      }
+    }
+    if (cur_bh >= 0 && ok) flush(cur_bh);
+    if (!ok && lane == 0) {
+      atomicCAS(g.status, kErrNone, kErrTimeoutEpilogue);
+      pair_abort(abort_flag);
+      atomicExch(g.valid, 0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1 && leader && lane == 0 && *reinterpret_cast<volatile int*>(abort_flag)) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(drain))
+                 : "memory");
+    mbar_wait(drain, 0);
+  }
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(Q_TMEM_COLS) : "memory");
+  }
+}
+
 // 4-D tensor map over [B][H][S][D] with element strides (sb, sh, ss) and box QBK x rows x 1 x 1.
 int encode_qk_map(CUtensorMap* map, const void* base, int dtype, int64_t d, int64_t s, int64_t h, int64_t b,
                   int64_t ss, int64_t sh, int64_t sb, int rows) {
@@ -261,9 +582,72 @@ __device__ int32_t g_qk_status;
 
 // Tensor-core path of muzo_qk_max (bf16 / fp16, strides multiple of 8 elements). enc holds the
 // head maxima as ordered integers, already initialised by the caller.
+// CTA-pair launch (head dim up to 256): contiguous tile ranges over min(tiles, co-resident pairs).
+int qk_max_pair(const void* q, const void* k, int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t sq,
+                int64_t sk, int64_t d, int64_t qsb, int64_t qsh, int64_t qss, int64_t ksb, int64_t ksh, int64_t kss,
+                int causal, int* enc, int32_t* valid, cudaStream_t stream) {
+  CUtensorMap mq, mk;
+  int st = encode_qk_map(&mq, q, dtype, d, sq, hq, batch, qss, qsh, qsb, PQ_ROWS);
+  if (st != MUZO_OK) return st;
+  st = encode_qk_map(&mk, k, dtype, d, sk, hkv, batch, kss, ksh, ksb, PK_ROWS);
+  if (st != MUZO_OK) return st;
+  QkPairArgs g;
+  g.sq = sq; g.sk = sk; g.shift = sk - sq;
+  g.hq = static_cast<int>(hq); g.group = static_cast<int>(hq / hkv);
+  g.nqb = static_cast<int>((sq + 2 * PQ_ROWS - 1) / (2 * PQ_ROWS));
+  g.causal = causal;
+  g.num_kb = static_cast<int>((d + QBK - 1) / QBK);
+  g.k_stages = (PQK_TILE_BYTES - PQ_SLOTS * g.num_kb * PQ_SUB_BYTES) / PK_STAGE_BYTES;
+  if (g.k_stages > PK_MAX_STAGES) g.k_stages = PK_MAX_STAGES;
+  int64_t per = 0;
+  for (int qb = 0; qb < g.nqb; ++qb) {
+    int64_t end = sk;
+    if (causal) {
+      const int64_t last = static_cast<int64_t>(qb + 1) * 2 * PQ_ROWS + g.shift;
+      end = last < sk ? last : sk;
+      if (end < 0) end = 0;
+    }
+    per += (end + 2 * PK_ROWS - 1) / (2 * PK_ROWS);
+  }
+  g.tiles_per_bh = per;
+  g.num_tiles = per * batch * hq;
+  g.enc = enc;
+  g.valid = valid;
+  void* p = nullptr;
+  MUZO_CUDA_CHECK(cudaGetSymbolAddress(&p, g_qk_status));
+  g.status = static_cast<int32_t*>(p);
+  if (g.num_tiles == 0) return MUZO_OK;
+  auto kern = dtype == MUZO_BF16 ? qk_max_pair_kernel<1> : qk_max_pair_kernel<0>;
+  static int max_pairs[2][64] = {{0}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return MUZO_ERR_UNSUPPORTED;
+  const int fi = dtype == MUZO_BF16 ? 1 : 0;
+  if (max_pairs[fi][dev] == 0) {
+    MUZO_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PQK_SMEM_BYTES));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * (device_sm_count() / 2)), 1, 1);
+    cfg.blockDim = dim3(PQK_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = PQK_SMEM_BYTES;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      clusters = device_sm_count() / 2;
+    }
+    max_pairs[fi][dev] = clusters;
+  }
+  const int64_t pairs = g.num_tiles < max_pairs[fi][dev] ? g.num_tiles : max_pairs[fi][dev];
+  kern<<<static_cast<unsigned>(2 * pairs), PQK_THREADS, PQK_SMEM_BYTES, stream>>>(mq, mk, g);
+  return launch_status();
+}
+
 int qk_max_tensor_cores(const void* q, const void* k, int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t sq,
                         int64_t sk, int64_t d, int64_t qsb, int64_t qsh, int64_t qss, int64_t ksb, int64_t ksh,
                         int64_t kss, int causal, int* enc, int32_t* valid, cudaStream_t stream) {
+  const char* pv = std::getenv("MUZO_QK_PAIR");
+  if (d <= PQ_MAX_KB * QBK && !(pv != nullptr && pv[0] == '0'))
+    return qk_max_pair(q, k, dtype, batch, hq, hkv, sq, sk, d, qsb, qsh, qss, ksb, ksh, kss, causal, enc, valid,
+                       stream);
   CUtensorMap mq, mk;
   int st = encode_qk_map(&mq, q, dtype, d, sq, hq, batch, qss, qsh, qsb, QM);
   if (st != MUZO_OK) return st;

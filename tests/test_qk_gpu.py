@@ -18,11 +18,20 @@ def _ulp(x: torch.Tensor, bits: int) -> torch.Tensor:
     return torch.pow(2.0, torch.floor(torch.log2(ax)) - bits)
 
 
+@pytest.fixture(params=["pair", "single"])
+def qk_kernel(request, monkeypatch):
+    """bf16 / fp16 run on the CTA-pair kernel (256 x 256 tiles, query block resident) unless
+    MUZO_QK_PAIR=0 selects the one-SM kernel: both are checked."""
+    monkeypatch.setenv("MUZO_QK_PAIR", "1" if request.param == "pair" else "0")
+    return request.param
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("b,hq,hkv,sq,sk,d", [(2, 8, 2, 100, 100, 64), (1, 4, 4, 64, 64, 128), (2, 6, 1, 33, 70, 32),
-                                             (1, 8, 2, 1000, 1000, 128), (1, 2, 1, 300, 700, 96)])
-def test_qk_max_matches_eager_logits(device, dtype, causal, b, hq, hkv, sq, sk, d):
+                                             (1, 8, 2, 1000, 1000, 128), (1, 2, 1, 300, 700, 96),
+                                             (1, 4, 1, 520, 520, 256), (3, 2, 2, 257, 257, 64)])
+def test_qk_max_matches_eager_logits(device, qk_kernel, dtype, causal, b, hq, hkv, sq, sk, d):
     from muzo_clip_b200 import _qk
 
     g = torch.Generator(device="cpu").manual_seed(b * 100 + hq + sq)
@@ -39,14 +48,18 @@ def test_qk_max_matches_eager_logits(device, dtype, causal, b, hq, hkv, sq, sk, 
     assert bool(((got - ref).abs() <= _ulp(ref, bits)).all()), (got, ref)
 
 
-def test_qk_max_flags_nonfinite(device):
+@pytest.mark.parametrize("bad", [float("inf"), float("-inf"), float("nan")])
+def test_qk_max_flags_nonfinite(device, qk_kernel, bad):
     from muzo_clip_b200 import _qk
 
-    q = torch.randn((1, 2, 16, 32), device=device, dtype=torch.bfloat16)
-    k = torch.randn((1, 2, 16, 32), device=device, dtype=torch.bfloat16)
-    q[0, 1, 3, 5] = float("inf")
+    q = torch.randn((1, 2, 300, 64), device=device, dtype=torch.bfloat16)
+    k = torch.randn((1, 2, 300, 64), device=device, dtype=torch.bfloat16)
+    q[0, 1, 3, 5] = bad
     _, valid = _qk.qk_head_max(q, k, 0.2, True, None)
     assert int(valid.item()) == 0
+    q[0, 1, 3, 5] = 0.0
+    _, valid = _qk.qk_head_max(q, k, 0.2, True, None)
+    assert int(valid.item()) == 1
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
