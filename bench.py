@@ -147,9 +147,9 @@ class ClockSampler:
 # DRAM traffic measured by one ncu capture of this workload on one B200 (1-pass metrics
 # gpu__time_duration.sum, dram__bytes_read.sum, dram__bytes_write.sum, --clock-control none, on
 # `python bench.py --steps 1 --warmup 1 --no-cpu-baseline`): read + write summed over the 105
-# ns_gemm launches of one step (960.3 GB over the 2 captured steps), and per perturbation pass.
-NS_DRAM_BYTES_PER_STEP = 480.2e9
-PERTURB_DRAM_BYTES_PER_PASS = 27.86e9
+# ns_gemm launches of one step (794.4 GB over the 2 captured steps), and per perturbation pass.
+NS_DRAM_BYTES_PER_STEP = 397.2e9
+PERTURB_DRAM_BYTES_PER_PASS = 27.89e9
 
 
 def ns_operand_bytes(rows: int, cols: int, steps: int = 5) -> float:
