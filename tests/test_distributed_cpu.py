@@ -8,7 +8,6 @@ ranks; the SPSA losses are averaged over the group so every rank derives the sam
 from __future__ import annotations
 
 import os
-import socket
 import sys
 from pathlib import Path
 
@@ -20,21 +19,15 @@ import torch.multiprocessing as mp
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 class _Block:
     def __init__(self, index, rows, cols, tensor):
         self.index, self.rows, self.cols, self.tensor, self.dtype = index, rows, cols, tensor, tensor.dtype
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+def _worker(rank: int, world: int, store: str, out_dir: str) -> None:
     sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # file rendezvous: no TCP port to race for on a shared host
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=world)
     try:
         from muzo_clip_b200._engine import ns_flops, partition_blocks
         from muzo_clip_b200.distributed import ShardedStepEngine
@@ -103,7 +96,8 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
 
 def test_sharded_collectives_on_two_gloo_ranks(tmp_path):
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, str(tmp_path / "store"), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
     lines = [Path(tmp_path, f"rank{r}.txt").read_text().split(" ", 3) for r in range(world)]
     for ok, stats_ok, same_p, owner in lines:
         assert ok == "1" and stats_ok == "1" and same_p == "1"

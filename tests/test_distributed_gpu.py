@@ -9,7 +9,6 @@ partition and the batch composition change nothing. Skipped with fewer than 2 GP
 from __future__ import annotations
 
 import os
-import socket
 import sys
 from datetime import timedelta
 from pathlib import Path
@@ -22,12 +21,6 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parent.parent
 SHAPES = [(512, 256), (256, 512), (1024, 256), (384, 384), (256, 768), (768, 256), (512, 256), (256, 256)]
 STEPS = 6
-
-
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
 
 
 def _build(device):
@@ -57,14 +50,15 @@ def _run(model, process_group=None) -> dict[str, torch.Tensor]:
     return {n: p.detach().cpu() for n, p in model.named_parameters()}
 
 
-def _worker(rank: int, world: int, port: int, out_prefix: str) -> None:
+def _worker(rank: int, world: int, store: str, out_prefix: str) -> None:
     sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
 
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
+    # file rendezvous: no TCP port to race for on a shared host
+    dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
     try:
         weights = _run(_build(torch.device("cuda", rank)), dist.group.WORLD)
         torch.save(weights, f"{out_prefix}.{rank}")
@@ -78,8 +72,8 @@ def test_two_ranks_match_one_gpu(tmp_path):
     import torch.multiprocessing as mp
 
     ref = _run(_build(torch.device("cuda", 0)))
-    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path / "w")), nprocs=2, start_method="spawn",
-                       join=True)
+    mp.start_processes(_worker, args=(2, str(tmp_path / "store"), str(tmp_path / "w")), nprocs=2,
+                       start_method="spawn", join=True)
     moved = sum(int(not torch.equal(ref[n], v)) for n, v in _build(torch.device("cpu")).named_parameters())
     assert moved == len(SHAPES)  # every selected matrix was updated
     for r in range(2):
