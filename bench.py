@@ -311,6 +311,12 @@ def run_gpu(args) -> int:
         clk = clocks.summary()
         n_elems = total_numel(args.layers)
         ns_bytes_min = sum(ns_operand_bytes(b.rows, b.cols) for b in engine.owned)
+        owned_elems = sum(b.rows * b.cols for b in engine.owned)
+        rebuild_ms = max(phases.get("rebuild", 0.0), 1e-9)
+        rebuild_samples = float(HORIZON) * owned_elems
+        rebuild_bytes = 4.0 * owned_elems
+        update_ms = max(phases.get("normalize", 0.0) + phases.get("apply", 0.0), 1e-9)
+        update_bytes = 12.0 * owned_elems
         h2d = 8 * len(engine.blocks) * 3 + 8 * len(engine.owned) * HORIZON + 4 * HORIZON
         d2h = engine.state_bytes + 16
         line = {
@@ -357,6 +363,21 @@ def run_gpu(args) -> int:
                 "rademacher_achieved": round(rad_gbs, 1), "rademacher_frac": round(rad_gbs / peaks["hbm_gbs"], 4),
                 "traffic": PERTURB_DRAM_BYTES_PER_PASS, "traffic_unit": "DRAM bytes per pass (ncu)",
                 "algorithmic_bytes": perturb_bytes,
+            },
+            # the rebuild regenerates H normal samples per weight: its bound is the instruction
+            # issue rate (ncu: 43 instructions per sample, 74 % issue utilisation), not HBM
+            "rebuild_roofline": {
+                "bound": "issue", "achieved": round(rebuild_samples / (rebuild_ms * 1e-3) / 1e9, 1),
+                "unit": "G normal samples/s", "hbm_achieved": round(rebuild_bytes / (rebuild_ms * 1e-3) / 1e9, 1),
+                "hbm_frac": round(rebuild_bytes / (rebuild_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                "algorithmic_bytes": rebuild_bytes,
+            },
+            # normalisation (bf16 read + write), the update's sum of squares (bf16 read) and the
+            # apply (update and W read, W written): 12 B per owned weight
+            "update_roofline": {
+                "bound": "hbm", "achieved": round(update_bytes / (update_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "peak": peaks["hbm_gbs"], "frac": round(update_bytes / (update_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                "algorithmic_bytes": update_bytes,
             },
             "e2e": {"value": round(wall_ms, 3), "unit": "ms/step", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
