@@ -7,6 +7,8 @@
 #include <string>
 #include <vector>
 
+#include <atomic>
+
 #include "muzo_b200.h"
 
 namespace muzo {
@@ -16,16 +18,16 @@ static thread_local int g_last_cuda_error = 0;
 void set_last_cuda_error(cudaError_t err) { g_last_cuda_error = static_cast<int>(err); }
 
 int device_sm_count() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int v = 0;
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
       v = 148;
-    cached[dev] = v;
+    cached[dev].store(v, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return v;
 }
 
 // ------------------------------------------------------------------ BLAKE2b (RFC 7693)

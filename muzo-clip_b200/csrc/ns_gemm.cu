@@ -14,6 +14,7 @@
 //               256-column TMEM accumulators, so the epilogue of tile i overlaps tile i+1;
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, apply the fused op, store bf16.
 // Every wait is bounded; on timeout the kernel records an error code, drains and returns.
+#include <atomic>
 #include <cstdlib>
 
 #include "tcgen05_common.cuh"
@@ -613,12 +614,12 @@ int encode_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, 
 template <bool A_MN, bool B_MN, int EPI>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, cudaStream_t s) {
   auto kern = ns_gemm_kernel<A_MN, B_MN, EPI>;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev >= 0 && dev < 64 && !configured[dev].load(std::memory_order_acquire)) {
     MUZO_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    configured[dev] = true;
+    configured[dev].store(true, std::memory_order_release);
   }
   int64_t grid = g.num_tiles < device_sm_count() ? g.num_tiles : device_sm_count();
   kern<<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, s>>>(ma, mb, g);
@@ -630,11 +631,11 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
 template <bool A_MN, bool B_MN, int EPI>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, cudaStream_t s) {
   auto kern = ns_gemm_pair_kernel<A_MN, B_MN, EPI>;
-  static int max_pairs[64] = {0};
+  static std::atomic<int> max_pairs[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return MUZO_ERR_UNSUPPORTED;
-  if (max_pairs[dev] == 0) {
+  if (max_pairs[dev].load(std::memory_order_acquire) == 0) {
     MUZO_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * (device_sm_count() / 2)), 1, 1);
@@ -645,9 +646,10 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
       cudaGetLastError();
       clusters = device_sm_count() / 2;
     }
-    max_pairs[dev] = clusters;
+    max_pairs[dev].store(clusters, std::memory_order_release);
   }
-  const int64_t pairs = g.num_tiles < max_pairs[dev] ? g.num_tiles : max_pairs[dev];
+  const int64_t cap = max_pairs[dev].load(std::memory_order_acquire);
+  const int64_t pairs = g.num_tiles < cap ? g.num_tiles : cap;
   kern<<<static_cast<unsigned>(2 * pairs), NUM_THREADS, P_SMEM_BYTES, s>>>(ma, mb, g);
   return launch_status();
 }

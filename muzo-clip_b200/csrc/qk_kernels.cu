@@ -153,12 +153,11 @@ logits_head_max_kernel(const char* __restrict__ logits, int64_t bsz, int64_t hea
 
 // The tensor-core path can be turned off for comparison runs (MUZO_QK_SIMT=1).
 bool qk_tensor_cores_enabled() {
-  static int enabled = -1;
-  if (enabled < 0) {
+  static const bool enabled = [] {
     const char* e = getenv("MUZO_QK_SIMT");
-    enabled = (e != nullptr && e[0] == '1') ? 0 : 1;
-  }
-  return enabled == 1;
+    return !(e != nullptr && e[0] == '1');
+  }();
+  return enabled;
 }
 
 __global__ void max_merge_kernel(float* running, const float* fresh, const int32_t* valid, int n) {

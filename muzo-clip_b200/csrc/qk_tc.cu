@@ -11,6 +11,7 @@
 // Layout of the kernel follows the Newton-Schulz GEMM: persistent CTAs (one per SM), warp 0 TMA
 // producer into a 4-stage ring, warp 1 TMEM owner and MMA issuer with two 256-column
 // accumulators, warps 2-5 epilogue; every wait is bounded.
+#include <atomic>
 #include <cstdlib>
 
 #include "tcgen05_common.cuh"
@@ -618,12 +619,12 @@ int qk_max_pair(const void* q, const void* k, int dtype, int64_t batch, int64_t 
   g.status = static_cast<int32_t*>(p);
   if (g.num_tiles == 0) return MUZO_OK;
   auto kern = dtype == MUZO_BF16 ? qk_max_pair_kernel<1> : qk_max_pair_kernel<0>;
-  static int max_pairs[2][64] = {{0}};
+  static std::atomic<int> max_pairs[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return MUZO_ERR_UNSUPPORTED;
   const int fi = dtype == MUZO_BF16 ? 1 : 0;
-  if (max_pairs[fi][dev] == 0) {
+  if (max_pairs[fi][dev].load(std::memory_order_acquire) == 0) {
     MUZO_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PQK_SMEM_BYTES));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * (device_sm_count() / 2)), 1, 1);
@@ -634,9 +635,10 @@ int qk_max_pair(const void* q, const void* k, int dtype, int64_t batch, int64_t 
       cudaGetLastError();
       clusters = device_sm_count() / 2;
     }
-    max_pairs[fi][dev] = clusters;
+    max_pairs[fi][dev].store(clusters, std::memory_order_release);
   }
-  const int64_t pairs = g.num_tiles < max_pairs[fi][dev] ? g.num_tiles : max_pairs[fi][dev];
+  const int64_t cap = max_pairs[fi][dev].load(std::memory_order_acquire);
+  const int64_t pairs = g.num_tiles < cap ? g.num_tiles : cap;
   kern<<<static_cast<unsigned>(2 * pairs), PQK_THREADS, PQK_SMEM_BYTES, stream>>>(mq, mk, g);
   return launch_status();
 }
@@ -678,13 +680,13 @@ int qk_max_tensor_cores(const void* q, const void* k, int dtype, int64_t batch, 
   g.status = static_cast<int32_t*>(p);
   if (g.num_tiles == 0) return MUZO_OK;
   auto kern = dtype == MUZO_BF16 ? qk_max_tc_kernel<1> : qk_max_tc_kernel<0>;
-  static bool configured[2][64] = {{false}};
+  static std::atomic<bool> configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   const int fi = dtype == MUZO_BF16 ? 1 : 0;
-  if (dev >= 0 && dev < 64 && !configured[fi][dev]) {
+  if (dev >= 0 && dev < 64 && !configured[fi][dev].load(std::memory_order_acquire)) {
     MUZO_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Q_SMEM_BYTES));
-    configured[fi][dev] = true;
+    configured[fi][dev].store(true, std::memory_order_release);
   }
   const int64_t grid = g.num_tiles < device_sm_count() ? g.num_tiles : device_sm_count();
   kern<<<static_cast<unsigned>(grid), Q_THREADS, Q_SMEM_BYTES, stream>>>(mq, mk, g);

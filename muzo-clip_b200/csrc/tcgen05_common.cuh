@@ -263,15 +263,16 @@ __device__ __forceinline__ void pair_abort(int* flag) {
     asm volatile("st.release.cluster.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank(a, r)), "r"(1) : "memory");
 }
 
+// The driver's tensor-map encoder, looked up once (thread-safe static initialisation).
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    return nullptr;
+  }();
   return fn;
 }
 
