@@ -287,12 +287,14 @@ class StepEngine:
 
     def owned_ns_flops_executed(self) -> float:
         """FLOPs the tensor cores execute: X X^T and b A + c A A only on the tiles that meet the
-        upper triangle (128 x 256 tiles), a X + B X in full."""
+        upper triangle (256 x 256 CTA-pair tiles for m >= 256, else 128 x 256 one-SM tiles),
+        a X + B X in full."""
         tot = 0.0
         for b in self.owned:
             m, n = min(b.rows, b.cols), max(b.rows, b.cols)
-            tm, tn = -(-m // 128), -(-m // 256)
-            frac = sum(tn - (r * 128) // 256 for r in range(tm)) / float(tm * tn)
+            bm = 256 if m >= 256 else 128
+            tm, tn = -(-m // bm), -(-m // 256)
+            frac = sum(tn - (r * bm) // 256 for r in range(tm)) / float(tm * tn)
             tot += self.opt.ns_steps * (frac * (2.0 * m * m * n + 2.0 * m ** 3) + 2.0 * m * m * n)
         return tot
 
