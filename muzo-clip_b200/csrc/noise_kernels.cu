@@ -133,7 +133,9 @@ fill_noise_kernel(const muzo_segment* __restrict__ segs, int nsegs, uint64_t key
       if (vec && li + 8 <= sv.numel) {
         store8(sv.out, li, odtype, z[j]);
       } else {
-        for (int k = 0; k < 8 && li + k < sv.numel; ++k) store_elem(sv.out, li + k, odtype, z[j][k]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)  // static indices keep the arrays in registers
+          if (li + k < sv.numel) store_elem(sv.out, li + k, odtype, z[j][k]);
       }
     }
   }
@@ -214,12 +216,18 @@ perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
           if (!kHoist) raw[j].load(sv.param, li);
           raw[j].unpack(w);
         } else {
+#pragma unroll
           for (int k = 0; k < 8; ++k) w[k] = k < cnt ? load_elem(sv.param, li + k, DTYPE) : 0.0f;
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) w[k] = __fadd_rn(w[k], ((sbits[j] >> k) & 1u) ? alpha : -alpha);
-        if (vec && cnt == 8) store8(sv.param, li, DTYPE, w);
-        else for (int k = 0; k < cnt; ++k) store_elem(sv.param, li + k, DTYPE, w[k]);
+        if (vec && cnt == 8) {
+          store8(sv.param, li, DTYPE, w);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)  // static indices keep w in registers
+            if (k < cnt) store_elem(sv.param, li + k, DTYPE, w[k]);
+        }
       }
     } else {
       // normal noise: bound by the Box-Muller arithmetic; weights loaded after it
@@ -238,9 +246,12 @@ perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
           for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, z[j][k], w[k]);
           store8(sv.param, li, DTYPE, w);
         } else {
-          for (int k = 0; k < 8 && li + k < sv.numel; ++k) {
-            const float w = load_elem(sv.param, li + k, DTYPE);
-            store_elem(sv.param, li + k, DTYPE, __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w));
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {  // static indices keep z in registers
+            if (li + k < sv.numel) {
+              const float w = load_elem(sv.param, li + k, DTYPE);
+              store_elem(sv.param, li + k, DTYPE, __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w));
+            }
           }
         }
       }
@@ -366,8 +377,11 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
         load4(sv.param, li, PDTYPE, w);
         store4_bf16(sv.out, li, m);
       } else {
+#pragma unroll
         for (int k = 0; k < 4; ++k) w[k] = k < cnt ? load_elem(sv.param, li + k, PDTYPE) : 0.0f;
-        for (int k = 0; k < cnt; ++k) store_elem(sv.out, li + k, MUZO_BF16, m[k]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // static indices keep m in registers
+          if (k < cnt) store_elem(sv.out, li + k, MUZO_BF16, m[k]);
       }
       float pm = 0.0f, px = 0.0f, pw = 0.0f;
       float mb[4] = {m[0], m[1], m[2], m[3]};

@@ -76,8 +76,10 @@ ns_normalize_kernel(const muzo_segment* __restrict__ segs, int nsegs, const doub
       for (int k = 0; k < 8; ++k) x[k] = __fdiv_rn(x[k], denom);
       store8(v.out, li, MUZO_BF16, x);
     } else {
-      for (int k = 0; k < 8 && li + k < v.numel; ++k)
-        store_elem(v.out, li + k, MUZO_BF16, __fdiv_rn(load_elem(v.out, li + k, MUZO_BF16), denom));
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (li + k < v.numel)
+          store_elem(v.out, li + k, MUZO_BF16, __fdiv_rn(load_elem(v.out, li + k, MUZO_BF16), denom));
     }
   }
 }
@@ -112,7 +114,11 @@ ns_prepare_kernel(const muzo_segment* __restrict__ segs, int nsegs, double* __re
     }
     m2 += pm; x2 += px;
     if (vec && cnt == 8) store8(v.out, li, MUZO_BF16, g);
-    else for (int k = 0; k < cnt; ++k) store_elem(v.out, li + k, MUZO_BF16, g[k]);
+    else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < cnt) store_elem(v.out, li + k, MUZO_BF16, g[k]);
+    }
   }
   double* bs = sums + static_cast<int64_t>(v.block) * MUZO_NSUMS;
   const double tm = block_sum(m2);
@@ -231,7 +237,11 @@ apply_update_kernel(const muzo_segment* __restrict__ segs, int nsegs, const floa
     }
     acc += p;
     if (vec && cnt == 8) store8(v.param, li, DTYPE, w);
-    else for (int k = 0; k < cnt; ++k) store_elem(v.param, li + k, DTYPE, w[k]);
+    else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)  // static indices keep w in registers
+        if (k < cnt) store_elem(v.param, li + k, DTYPE, w[k]);
+    }
   }
   const double tot = block_sum(acc);
   if (threadIdx.x == 0 && tot != 0.0) atomicAdd(bs + MUZO_SUM_U2_CLIPPED, tot);
