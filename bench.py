@@ -172,39 +172,34 @@ def load_peaks() -> dict:
 # ---------------------------------------------------------------- CPU oracle baseline
 
 
-def cpu_sample_ms(seed: int = 0) -> tuple[float, str, int]:
-    """Time the oracle on one k_proj-shaped block (1024x4096) through the whole step (three
-    perturbation passes, H=8 rebuild, Newton-Schulz, update) and extrapolate to the full 8B
-    step: element-wise phases by element count, Newton-Schulz by FLOPs."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import muzo_oracle as orc
+def _extrapolate_ms(wall: float, phases: list, workers: int) -> float:
+    """Per-step milliseconds of the 8B step from one batch of `workers` blocks run at once: the
+    batch's wall time per block, split by the blocks' own phase times; element-wise phases
+    scale by element count, Newton-Schulz by FLOPs."""
+    from cpu_baseline import COLS, ROWS
 
-    rows, cols = KV, HIDDEN
-    rng = np.random.default_rng(seed)
-    w = (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02)
-    w = orc.bf16_round(w)
-    keys = [int(k) for k in rng.integers(0, 2**63 - 1, size=HORIZON + 1, dtype=np.int64)]
-    ps = np.clip(rng.standard_normal(HORIZON), -3, 3)
-    t0 = time.perf_counter()
-    for alpha in (1e-3, -2e-3, 1e-3):
-        w = orc.perturb(w, keys[0], alpha, "normal", "bf16")
-    t1 = time.perf_counter()
-    coeffs = [0.9 ** a for a in range(HORIZON)]
-    m = orc.rebuild((rows, cols), keys[1:], [c * p for c, p in zip(coeffs, ps)], "normal", "bf16",
-                    float(np.float32(1.0) / np.float32(sum(coeffs))))
-    t2 = time.perf_counter()
-    x = orc.ns5_bf16(m, 5)
-    t3 = time.perf_counter()
-    orc.apply_update(w, x, 1e-5, 0.2, 0.01, 0.01, "bf16")
-    t4 = time.perf_counter()
-    elem_scale = total_numel() / (rows * cols)
-    m_, n_ = min(rows, cols), max(rows, cols)
+    tot = np.sum(np.asarray(phases, dtype=np.float64), axis=0)
+    frac = tot / max(float(tot.sum()), 1e-12)
+    elem_scale = total_numel() / (ROWS * COLS)
+    m_, n_ = min(ROWS, COLS), max(ROWS, COLS)
     flop_scale = ns_flops_total() / (5 * (4.0 * m_ * m_ * n_ + 2.0 * m_ ** 3))
-    est_s = ((t1 - t0) + (t2 - t1) + (t4 - t3)) * elem_scale + (t3 - t2) * flop_scale
-    sample = (f"oracle on one 1024x4096 bf16 block (3 perturb passes, H=8 normal rebuild, NS5, apply) in "
-              f"{t4 - t0:.1f} s; extrapolated to 224 matrices (elementwise x{elem_scale:.0f}, NS by FLOPs x{flop_scale:.0f})")
-    threads = os.cpu_count() or 1
-    return est_s * 1e3, sample, threads
+    return 1e3 * (wall / workers) * ((frac[0] + frac[1] + frac[3]) * elem_scale + frac[2] * flop_scale)
+
+
+def _sample_text(workers: int, walls: list[float]) -> str:
+    return (f"oracle, one 1024x4096 bf16 block per host core ({workers} blocks per batch, one thread each: "
+            f"3 perturb passes, H=8 normal rebuild, NS5, apply; batch wall {', '.join(f'{w:.1f}' for w in walls)} s); "
+            f"extrapolated to 224 matrices (element-wise by element count x1664, NS by FLOPs x6891)")
+
+
+def cpu_sample_ms(seed: int = 0) -> tuple[float, str, int]:
+    """The oracle (numpy restatement of the reference's arithmetic) through the whole step on
+    all host cores at once (one k_proj-shaped block per core), extrapolated to the 8B step."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from cpu_baseline import throughput_sample
+
+    wall, phases, workers = throughput_sample(seed)
+    return _extrapolate_ms(wall, phases, workers), _sample_text(workers, [wall]), workers
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -400,14 +395,21 @@ def run_reference(args) -> int:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    threads = os.cpu_count() or 1
-    vals = []
-    sample = ""
-    for i in range(args.warmup + args.steps):
-        ms, sample, threads = cpu_sample_ms(seed=i)
-        if i >= args.warmup:
-            vals.append(ms)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from cpu_baseline import HostPool
+
+    # each step is one batch of ~10-30 s on all cores: at most one untimed and three timed
+    # batches, whatever --steps / --warmup ask, so the arm ends within a few minutes
+    vals, walls = [], []
+    with HostPool() as pool:
+        threads = pool.workers
+        for i in range(min(args.warmup, 1) + min(args.steps, 3)):
+            wall, phases = pool.batch(seed=i * pool.workers)
+            if i >= min(args.warmup, 1):
+                vals.append(_extrapolate_ms(wall, phases, pool.workers))
+                walls.append(wall)
     v = statistics.median(vals)
+    sample = _sample_text(threads, walls) + f"; median of {len(vals)} batches"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "ms/step", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1), "higher_is_better": False,
