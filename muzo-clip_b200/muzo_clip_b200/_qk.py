@@ -54,18 +54,8 @@ def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: 
 
         group = query.shape[1] // key.shape[1]
         kr = key.repeat_interleave(group, dim=1)
-        if attention_mask.dtype == torch.bool:  # SDPA's boolean form -> eager's additive form
-            keep = attention_mask
-            if causal:
-                # transformers un-masks rows that would be fully masked (padding queries) so that
-                # SDPA returns no NaN; eager attention keeps them masked: in a causal model such
-                # a row is the one that sees a key above the diagonal
-                sq_, sk_ = keep.shape[-2], keep.shape[-1]
-                i = torch.arange(sq_, device=keep.device)[:, None] + (sk_ - sq_)
-                above = torch.arange(sk_, device=keep.device)[None, :] > i
-                keep = keep & ~(keep & above).any(dim=-1, keepdim=True)
-            attention_mask = torch.zeros(keep.shape, dtype=query.dtype, device=query.device).masked_fill(
-                ~keep, torch.finfo(query.dtype).min)
+        if attention_mask.dtype == torch.bool:
+            attention_mask = eager_additive_mask(attention_mask, causal, query.dtype)
         logits = torch.matmul(query, kr.transpose(2, 3)) * scaling + attention_mask
         return logits_head_max(logits)
     q, k = query, key
@@ -82,6 +72,19 @@ def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: 
                              1 if causal else 0, float(scaling), out.data_ptr(), valid.data_ptr(),
                              _lib.stream_ptr(q.device))
     return out, valid
+
+
+def eager_additive_mask(keep: torch.Tensor, causal: bool, dtype: torch.dtype) -> torch.Tensor:
+    """SDPA's boolean mask (True = attend) in eager attention's additive form (0 or the dtype's
+    minimum). transformers un-masks rows that would be fully masked (padding queries) so that SDPA
+    returns no NaN; eager attention keeps them masked. In a causal model such a row is the one
+    that sees a key above the (end-aligned) diagonal, and it is masked again here."""
+    if causal:
+        sq, sk = keep.shape[-2], keep.shape[-1]
+        i = torch.arange(sq, device=keep.device)[:, None] + (sk - sq)
+        above = torch.arange(sk, device=keep.device)[None, :] > i
+        keep = keep & ~(keep & above).any(dim=-1, keepdim=True)
+    return torch.zeros(keep.shape, dtype=dtype, device=keep.device).masked_fill(~keep, torch.finfo(dtype).min)
 
 
 def _is_plain_causal(mask: torch.Tensor, sq: int, sk: int) -> bool:
