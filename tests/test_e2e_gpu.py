@@ -1,7 +1,7 @@
-"""End to end on the tiny Llama of the reference's first benchmark configuration: 2 layers,
-hidden 256, 4 heads, MLP 688, vocab 1024, fp32, batch 4 x seq 64 token ids, README defaults,
-normal noise, 20 SPSA steps and one QK-Clip probe — the README's sanity checks
-(README.md:253-258) plus agreement of every update with the reference path."""
+"""End to end on a tiny Llama-style decoder: 2 layers, hidden 256, 4 heads, MLP 688, vocab
+1024, fp32, batch 4 x seq 64 token ids, the optimizer's default hyperparameters,
+normal noise, 20 SPSA steps and one QK-Clip probe — the sanity checks of the reference project's
+README.md:253-258, plus agreement of every update with the reference path."""
 
 from __future__ import annotations
 
