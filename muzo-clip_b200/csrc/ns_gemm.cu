@@ -6,7 +6,9 @@
 // tcgen05.mma.cta_group::2 over two SMs; default when both output extents are >= 256) and the
 // one-SM kernel below (128 x 256 tiles; small outputs). The pair kernel stages 32 KB of operands
 // per SM and k-block where the one-SM kernel stages 48 KB for the same flops: measured 7-8 %
-// faster on the 4096 x 4096 / 4096 x 14336 / 14336 x 4096 Newton-Schulz batches.
+// faster on the 4096 x 4096 / 4096 x 14336 / 14336 x 4096 Newton-Schulz batches. Its output
+// tiles are handed out in order by an atomic counter kept in the caller's status buffer, so
+// pairs delayed by other kernels on the GPU take fewer tiles.
 //
 // One-SM kernel: one persistent CTA per SM (grid = min(tiles, SMs)), 6 warps:
 //   warp 0      TMA producer (one thread): A/B k-blocks into a 4-stage shared-memory ring;
