@@ -28,6 +28,7 @@ import statistics
 import subprocess
 import sys
 import time
+from datetime import timedelta
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -213,8 +214,8 @@ def setup_dist():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=600))
+        # a rank that stops answering ends the others' next collective with an error
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
         return dist, rank, world, local
     torch.cuda.set_device(local)
     return None, 0, 1, local
