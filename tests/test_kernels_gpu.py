@@ -362,3 +362,30 @@ def test_step_matches_reference(device, dist, dtype):
             r_ref = _rel(refw - w0n, wi - w0n)
             assert r_mine <= r_ref + 2e-2, (r_mine, r_ref)
             assert float(np.mean(mine == wi)) >= 0.9, float(np.mean(mine == wi))
+
+
+def test_step_with_row_blocks_matches_reference_path(device):
+    """block_rows splits every matrix into row blocks, each with its own key, momentum,
+    Newton-Schulz and update (muzo_optimizer.py:316-357 over iter_param_blocks): fp32 weights
+    against the reference path on a twin, per-parameter relative update error within the
+    Newton-Schulz accumulation-order tolerance, same number of updated blocks."""
+    from muzo_clip_b200 import MuZOClipOptimizer
+    from muzo_clip_b200.muzo_optimizer import HistoryItem
+
+    model = _Mats([(688, 256), (300, 512)], torch.float32, device, seed=4)
+    twin = copy.deepcopy(model)
+    opt = MuZOClipOptimizer(model, distribution="normal", lr=1e-3, seed=2, block_rows=256)
+    hist = _history(5, seed=11)
+    for h in hist:
+        opt.history.append(HistoryItem(h.seed, h.p, 0.0, 0.0, 0.0))
+    opt._has_pending_update = True
+    before = [p.detach().clone() for p in model.parameters()]
+    stats = opt.step()
+    ref = tr.step(list(twin.named_parameters()), list(opt.history), lr=stats["lr"], beta=opt.beta_momentum,
+                  ns_steps=opt.ns_steps, muon_scale=opt.muon_scale, ratio_clip=opt.update_ratio_clip,
+                  weight_decay=opt.weight_decay, distribution="normal", block_rows=256)
+    assert stats["updated_param_count"] == ref["updated_param_count"] == 3 + 2
+    for b, p, q in zip(before, model.parameters(), twin.parameters()):
+        d_mine, d_ref = (p.detach() - b).float(), (q.detach() - b).float()
+        rel = ((d_mine - d_ref).norm() / d_ref.norm()).item()
+        assert rel < 6e-2, rel
