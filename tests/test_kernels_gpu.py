@@ -35,7 +35,7 @@ def _history(n, seed=0):
 
 @pytest.mark.parametrize("numel", [1, 7, 1000, 65539, 303104 * 4 + 17, 1 << 22])
 @pytest.mark.parametrize("dist", ["rademacher", "normal"])
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_noise_matches_torch_generator(device, numel, dist, dtype):
     from muzo_clip_b200 import make_zo_noise_like
 
@@ -103,7 +103,7 @@ def test_perturb_bit_exact(device, dist, dtype, block_rows):
 
 
 @pytest.mark.parametrize("dist", ["rademacher", "normal"])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
 @pytest.mark.parametrize("max_ctas", [0, 3])
 def test_rebuild_matches_reference_momentum(device, dist, dtype, max_ctas):
     L = _lib()
@@ -304,15 +304,15 @@ def _bf16_ulp(x: np.ndarray) -> np.ndarray:
 
 
 @pytest.mark.parametrize("dist", ["normal", "rademacher"])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
 def test_step_matches_reference(device, dist, dtype):
     """Full step() on four matrices. The momentum is bit-exact (rebuild test); the update is
     compared with the oracle's exact-accumulation Newton-Schulz of that momentum followed by the
     reference's scale / ratio-clip / apply / decay arithmetic, and with the reference's own
     cuBLAS path. fp32 weights: relative Frobenius error of the update <= 2e-2 against the exact
-    iteration, <= the reference's own deviation + 2e-2 against the reference. bf16 weights: the
-    update lands on the bf16 grid, so each weight must agree within 2 ulp + 2e-2 of its update,
-    90 % bit-equal."""
+    iteration, <= the reference's own deviation + 2e-2 against the reference. bf16 / fp16 weights:
+    the update lands on the weight grid; the stored update is no further from the exact iteration
+    than the reference's own cuBLAS path + 2e-2 (bf16: also >= 90 % of weights bit-equal)."""
     import muzo_oracle as orc
     from muzo_clip_b200 import MuZOClipOptimizer
     from muzo_clip_b200.muzo_optimizer import HistoryItem
@@ -327,7 +327,7 @@ def test_step_matches_reference(device, dist, dtype):
     before = [p.detach().clone() for p in model.parameters()]
     # oracle: exact momentum from the reference path, exact-accumulation NS, reference update math
     ideal_w, ideal_stats = [], []
-    odt = "bf16" if dtype == torch.bfloat16 else "f32"
+    odt = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[dtype]
     for name, w0 in zip(names, before):
         M = tr.rebuild(w0, name, 0, list(opt.history), opt.beta_momentum, dist, True).cpu().numpy()
         X = orc.ns5_bf16(M, opt.ns_steps, exact=True)
@@ -361,7 +361,8 @@ def test_step_matches_reference(device, dist, dtype):
             r_mine = _rel(mine - w0n, wi - w0n)
             r_ref = _rel(refw - w0n, wi - w0n)
             assert r_mine <= r_ref + 2e-2, (r_mine, r_ref)
-            assert float(np.mean(mine == wi)) >= 0.9, float(np.mean(mine == wi))
+            if dtype == torch.bfloat16:  # fp16's finer grid shows more of the 1-2 % spread in U
+                assert float(np.mean(mine == wi)) >= 0.9, float(np.mean(mine == wi))
 
 
 def test_step_with_row_blocks_matches_reference_path(device):
