@@ -390,3 +390,30 @@ def test_step_with_row_blocks_matches_reference_path(device):
         d_mine, d_ref = (p.detach() - b).float(), (q.detach() - b).float()
         rel = ((d_mine - d_ref).norm() / d_ref.norm()).item()
         assert rel < 6e-2, rel
+
+
+@pytest.mark.parametrize("kw", [dict(ns_steps=0), dict(ns_steps=1, normalize_momentum=False),
+                                dict(weight_decay=0.0, horizon=1, min_history=1)])
+def test_step_hyperparameter_edges_match_reference_path(device, kw):
+    """No Newton-Schulz iteration (the normalised momentum itself is the update), one iteration
+    without momentum normalisation, and a one-entry history without weight decay: fp32 weights
+    against the reference path on a twin."""
+    from muzo_clip_b200 import MuZOClipOptimizer
+    from muzo_clip_b200.muzo_optimizer import HistoryItem
+
+    model = _Mats([(256, 512), (384, 256)], torch.float32, device, seed=7)
+    twin = copy.deepcopy(model)
+    opt = MuZOClipOptimizer(model, distribution="normal", lr=1e-3, seed=4, **kw)
+    for h in _history(min(opt.horizon, 4), seed=13):
+        opt.history.append(HistoryItem(h.seed, h.p, 0.0, 0.0, 0.0))
+    opt._has_pending_update = True
+    before = [p.detach().clone() for p in model.parameters()]
+    stats = opt.step()
+    ref = tr.step(list(twin.named_parameters()), list(opt.history), lr=stats["lr"], beta=opt.beta_momentum,
+                  ns_steps=opt.ns_steps, muon_scale=opt.muon_scale, ratio_clip=opt.update_ratio_clip,
+                  weight_decay=opt.weight_decay, distribution="normal", normalize=opt.normalize_momentum)
+    assert stats["updated_param_count"] == ref["updated_param_count"] == 2
+    for b, p, q in zip(before, model.parameters(), twin.parameters()):
+        d_mine, d_ref = (p.detach() - b).float(), (q.detach() - b).float()
+        rel = ((d_mine - d_ref).norm() / d_ref.norm()).item()
+        assert rel < 6e-2, rel   # the Newton-Schulz accumulation-order tolerance of the other step tests
