@@ -3,7 +3,9 @@
 Every rank perturbs its own replica; each block is rebuilt, orthogonalised and applied by its
 owner only and broadcast to the others. With the same seeds and losses the weights must come out
 bit-identical on both ranks and equal to the single-GPU run: the kernels work per matrix, so the
-partition and the batch composition change nothing. Skipped with fewer than 2 GPUs.
+partition and the batch composition change nothing. With per-rank batches (each rank's closure
+returns its own loss) the ranks average the two SPSA losses, so they must match one GPU whose
+closure returns that mean. Skipped with fewer than 2 GPUs.
 """
 
 from __future__ import annotations
@@ -34,14 +36,26 @@ def _build(device):
     return model.to(device=device, dtype=torch.bfloat16)
 
 
-def _run(model, process_group=None) -> dict[str, torch.Tensor]:
+# per-rank batch offsets of the loss; 2-rank sums and halving are exact in fp64, so one GPU can
+# reproduce the all-reduced mean bit for bit
+RANK_SHIFT = (1.0, -1.0)
+
+
+def _run(model, process_group=None, shift=None) -> dict[str, torch.Tensor]:
+    """``shift``: None (same batch everywhere), a rank's own offset, or "mean" (one GPU playing
+    both ranks)."""
     from muzo_clip_b200 import MuZOClipOptimizer
 
     opt = MuZOClipOptimizer(model, seed=21, horizon=4, min_history=2, process_group=process_group)
     w0 = model.layers[0].up_proj.weight
 
     def closure():
-        return float(w0.float().square().sum().item())
+        f = float(w0.float().square().sum().item())
+        if shift is None:
+            return f
+        if shift == "mean":
+            return ((f + RANK_SHIFT[0]) + (f + RANK_SHIFT[1])) / 2.0
+        return f + shift
 
     for _ in range(STEPS):
         opt.estimate_projection(closure)
@@ -50,7 +64,7 @@ def _run(model, process_group=None) -> dict[str, torch.Tensor]:
     return {n: p.detach().cpu() for n, p in model.named_parameters()}
 
 
-def _worker(rank: int, world: int, store: str, out_prefix: str) -> None:
+def _worker(rank: int, world: int, store: str, out_prefix: str, own_batches: bool = False) -> None:
     sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
     os.environ.update(NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
@@ -60,19 +74,21 @@ def _worker(rank: int, world: int, store: str, out_prefix: str) -> None:
     dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
     try:
-        weights = _run(_build(torch.device("cuda", rank)), dist.group.WORLD)
+        weights = _run(_build(torch.device("cuda", rank)), dist.group.WORLD,
+                       RANK_SHIFT[rank] if own_batches else None)
         torch.save(weights, f"{out_prefix}.{rank}")
     finally:
         dist.destroy_process_group()
 
 
-def test_two_ranks_match_one_gpu(tmp_path):
+@pytest.mark.parametrize("own_batches", [False, True], ids=["same_batch", "per_rank_batches"])
+def test_two_ranks_match_one_gpu(tmp_path, own_batches):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
 
-    ref = _run(_build(torch.device("cuda", 0)))
-    mp.start_processes(_worker, args=(2, str(tmp_path / "store"), str(tmp_path / "w")), nprocs=2,
+    ref = _run(_build(torch.device("cuda", 0)), shift="mean" if own_batches else None)
+    mp.start_processes(_worker, args=(2, str(tmp_path / "store"), str(tmp_path / "w"), own_batches), nprocs=2,
                        start_method="spawn", join=True)
     moved = sum(int(not torch.equal(ref[n], v)) for n, v in _build(torch.device("cpu")).named_parameters())
     assert moved == len(SHAPES)  # every selected matrix was updated
