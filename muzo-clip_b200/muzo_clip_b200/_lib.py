@@ -25,6 +25,7 @@ lib = ctypes.CDLL(str(_LIB_PATH))
 
 # ---------------------------------------------------------------- ABI constants
 OK = 0
+ERR_ARG, ERR_DTYPE, ERR_ALIGN, ERR_CUDA, ERR_CAPACITY, ERR_UNSUPPORTED = 1, 2, 3, 4, 5, 6
 F32, BF16, F16 = 0, 1, 2
 NORMAL, RADEMACHER = 0, 1
 EPI_STORE, EPI_POLY, EPI_UPDATE = 0, 1, 2
@@ -127,7 +128,7 @@ def launch(name: str, *args) -> None:
 def check(status: int, what: str) -> None:
     if status != OK:
         msg = lib.muzo_status_string(status).decode()
-        if status == 4:
+        if status == ERR_CUDA:
             msg += f" (cudaError {lib.muzo_last_cuda_error()})"
         raise MuzoError(f"{what}: {msg}")
 
@@ -182,7 +183,7 @@ def plan_segments(numels, params, outs, dist: int, sm_count: int, max_threads: i
             out_arr.ctypes.data if out_arr is not None else None, n, dist, sm_count, max_threads,
             segs.ctypes.data, cap, _c.byref(nsegs), _c.byref(total),
         )
-        if st == 5:
+        if st == ERR_CAPACITY:
             cap *= 2
             continue
         check(st, "muzo_plan_segments")

@@ -36,6 +36,30 @@ def test_python_binding_covers_header():
     assert _lib.lib.muzo_abi_version() == 1
 
 
+def _header_constants() -> dict[str, int]:
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "muzo_b200.h").read_text(), flags=re.S)
+    found = dict(re.findall(r"\b(MUZO_[A-Z0-9_]+)\s*=\s*(\d+)", text))
+    found.update(re.findall(r"#define\s+(MUZO_[A-Z0-9_]+)\s+(\d+)", text))
+    return {k[len("MUZO_"):]: int(v) for k, v in found.items()}
+
+
+def test_python_constants_match_header():
+    """Every enum value and size the binding hard-codes equals the header's."""
+    from muzo_clip_b200 import _lib
+
+    consts = _header_constants()
+    assert len(consts) >= 30
+    checked = 0
+    for name, value in consts.items():
+        if name in ("ABI_VERSION", "NOALLOC_MAX_BLOCKS"):
+            continue
+        assert getattr(_lib, name) == value, name
+        checked += 1
+    assert checked == len(consts) - 2
+    assert _lib.lib.muzo_abi_version() == consts["ABI_VERSION"]
+    assert _lib.SEGMENT_DTYPE.itemsize == 64
+
+
 def test_hash_known_answers_native_and_python():
     from muzo_clip_b200 import _lib
     from muzo_clip_b200.prng import hash64_seed
