@@ -7,7 +7,8 @@ native library through ``_engine.StepEngine``.
 
 Two keyword arguments are additions: ``process_group`` shards the step over the ranks of a
 torch.distributed group (each rank rebuilds, orthogonalises and applies the blocks it owns, and
-NCCL broadcasts the updated weights; SPSA losses are averaged over the group), and
+NCCL broadcasts the updated weights; SPSA losses are averaged over the group and QK-Clip maxima
+max-reduced, so ranks may feed different batches), and
 ``workspace_bytes`` bounds the Newton-Schulz workspace.
 """
 
@@ -177,7 +178,8 @@ class MuZOClipOptimizer:
 
         self.qk_clip: QKClipController | None = None
         if enable_qk_clip:
-            self.qk_clip = QKClipController(model, tau=qk_clip_tau, alpha=qk_clip_alpha)
+            self.qk_clip = QKClipController(model, tau=qk_clip_tau, alpha=qk_clip_alpha,
+                                            process_group=process_group)
 
     # ------------------------------------------------------------------ public API
     @property

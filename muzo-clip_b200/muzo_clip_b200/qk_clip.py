@@ -13,6 +13,9 @@ reduces each to a per-head max with a host sync per layer (qk_clip.py:173-196). 
 * Maxima stay on the device until ``apply()``, which reads them in one copy and scales the q/k
   projection rows with the library's row-scaling kernel. Statistics and the GQA grouping rules
   follow qk_clip.py:198-322.
+* With a ``process_group`` (data-parallel ranks, each capturing on its own batch), ``apply()``
+  first takes the per-head maxima's maximum over the group, so every rank clips its replica
+  with the same factors and the replicas stay identical.
 """
 
 from __future__ import annotations
@@ -68,10 +71,11 @@ class QKClipApplyStats:
 class QKClipController:
     """Capture per-head pre-softmax maxima and apply QK-Clip to q/k projections."""
 
-    def __init__(self, model: torch.nn.Module, tau: float = 100.0, alpha: float = 0.5):
+    def __init__(self, model: torch.nn.Module, tau: float = 100.0, alpha: float = 0.5, process_group=None):
         self.model = model
         self.tau = float(tau)
         self.alpha = float(alpha)
+        self.process_group = process_group
         self.modules: dict[str, torch.nn.Module] = {}
         self._names_by_id: dict[int, str] = {}
         self._handles: list[Any] = []
@@ -242,9 +246,47 @@ class QKClipController:
 
     # ------------------------------------------------------------------ apply
     @torch.no_grad()
+    def reduce_over_group(self) -> None:
+        """Replace the captured maxima by their maximum over the process group (every rank must
+        call this together). Ranks may have captured different modules: a module captured on any
+        rank is present on all afterwards. Two all-reduces: the head count per module, then the
+        packed maxima (-inf where a rank has none)."""
+        pg = self.process_group
+        if pg is None or not self._installed:
+            return
+        import torch.distributed as dist
+
+        if dist.get_world_size(pg) <= 1:
+            return
+        names = list(self.modules)  # named_modules order: identical on identical replicas
+        first = next(iter(self.modules.values()))
+        device = first.q_proj.weight.device
+        counts = torch.tensor([self._captured_smax[n].numel() if n in self._captured_smax else 0 for n in names],
+                              dtype=torch.int64, device=device)
+        dist.all_reduce(counts, op=dist.ReduceOp.MAX, group=pg)
+        sizes = [int(c) for c in counts.tolist()]
+        packed = torch.full((max(sum(sizes), 1),), float("-inf"), dtype=torch.float32, device=device)
+        off = 0
+        for name, k in zip(names, sizes):
+            mine = self._captured_smax.get(name)
+            if mine is not None and mine.numel() != k:
+                raise ValueError(f"QK-Clip capture of {name}: {mine.numel()} heads on this rank, {k} on another")
+            if mine is not None:
+                packed[off: off + k].copy_(mine.reshape(-1))
+            off += k
+        dist.all_reduce(packed, op=dist.ReduceOp.MAX, group=pg)
+        self._captured_smax.clear()
+        off = 0
+        for name, k in zip(names, sizes):
+            if k:
+                self._captured_smax[name] = packed[off: off + k]
+            off += k
+
+    @torch.no_grad()
     def apply(self) -> QKClipApplyStats:
         if not self._installed:
             return QKClipApplyStats(False, False, False, "no q_proj/k_proj attention modules found", 0.0, 0)
+        self.reduce_over_group()
         if not self._captured_smax:
             reason = "QK-Clip disabled because pre-softmax logits are unavailable. Use attn_implementation='eager'."
             if not self._warned_unavailable:

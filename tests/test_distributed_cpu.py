@@ -2,7 +2,8 @@
 
 Covers: the LPT ownership is identical on every rank; owners' updated blocks reach every rank
 through the class-by-class broadcasts; per-block statistics combine to the same StepStats on all
-ranks; the SPSA losses are averaged over the group so every rank derives the same projection.
+ranks; the SPSA losses are averaged over the group so every rank derives the same projection;
+QK-Clip maxima captured on per-rank batches are max-reduced so every rank clips alike.
 """
 
 from __future__ import annotations
@@ -102,6 +103,46 @@ def test_sharded_collectives_on_two_gloo_ranks(tmp_path):
     for ok, stats_ok, same_p, owner in lines:
         assert ok == "1" and stats_ok == "1" and same_p == "1"
     assert lines[0][3] == lines[1][3]  # identical ownership on both ranks
+
+
+def _qk_worker(rank: int, world: int, store: str, out_dir: str) -> None:
+    sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=world)
+    try:
+        from muzo_clip_b200.qk_clip import QKClipController
+
+        model = torch.nn.Module()
+        model.layers = torch.nn.ModuleList()
+        for _ in range(3):
+            attn = torch.nn.Module()
+            attn.q_proj = torch.nn.Linear(8, 8, bias=False)
+            attn.k_proj = torch.nn.Linear(8, 4, bias=False)
+            model.layers.append(attn)
+        ctl = QKClipController(model, tau=1.0, process_group=dist.group.WORLD)
+        inf = float("inf")
+        # rank 0 saw layers 0 and 2, rank 1 saw layers 0 and 1 (e.g. a capture dropped for
+        # non-finite logits); -inf is a head with no visible logit
+        mine = {0: {"layers.0": [1.0, 5.0, 2.0, 3.0], "layers.2": [0.5, -inf]},
+                1: {"layers.0": [4.0, 0.0, 2.0, -inf], "layers.1": [7.0, 8.0, 9.0]}}[rank]
+        for name, vals in mine.items():
+            ctl._captured_smax[name] = torch.tensor(vals, dtype=torch.float32)
+        ctl.reduce_over_group()
+        got = {n: t.tolist() for n, t in ctl._captured_smax.items()}
+        want = {"layers.0": [4.0, 5.0, 2.0, 3.0], "layers.1": [7.0, 8.0, 9.0], "layers.2": [0.5, -inf]}
+        # nothing captured anywhere: stays empty on every rank
+        ctl.clear()
+        ctl.reduce_over_group()
+        Path(out_dir, f"qk{rank}.txt").write_text(f"{int(got == want)} {int(not ctl._captured_smax)}\n")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_qk_clip_maxima_reduced_over_two_gloo_ranks(tmp_path):
+    world = 2
+    mp.start_processes(_qk_worker, args=(world, str(tmp_path / "store"), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    for r in range(world):
+        assert Path(tmp_path, f"qk{r}.txt").read_text().split() == ["1", "1"], r
 
 
 def test_collective_order_is_global_for_any_ownership():

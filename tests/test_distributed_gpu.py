@@ -5,7 +5,9 @@ owner only and broadcast to the others. With the same seeds and losses the weigh
 bit-identical on both ranks and equal to the single-GPU run: the kernels work per matrix, so the
 partition and the batch composition change nothing. With per-rank batches (each rank's closure
 returns its own loss) the ranks average the two SPSA losses, so they must match one GPU whose
-closure returns that mean. Skipped with fewer than 2 GPUs.
+closure returns that mean. QK-Clip maxima captured on per-rank batches are max-reduced before
+the clip: both ranks' q/k weights must equal one GPU clipping with the element-wise maximum.
+Skipped with fewer than 2 GPUs.
 """
 
 from __future__ import annotations
@@ -96,3 +98,69 @@ def test_two_ranks_match_one_gpu(tmp_path, own_batches):
         got = torch.load(tmp_path / f"w.{r}")
         for name, value in ref.items():
             assert torch.equal(value, got[name]), (r, name)
+
+
+QK_MAXIMA = {  # per rank: module -> per-head maxima of its own batch (tau = 10)
+    0: {"layers.0": [12.0, 3.0, 30.0, 9.0], "layers.1": [1.0, 2.0, 3.0, 4.0]},
+    1: {"layers.0": [11.0, 25.0, 2.0, float("-inf")], "layers.2": [40.0, 5.0, 6.0, 7.0]},
+}
+
+
+def _qk_model(device):
+    torch.manual_seed(9)
+    model = torch.nn.Module()
+    model.layers = torch.nn.ModuleList()
+    for _ in range(3):
+        attn = torch.nn.Module()
+        attn.q_proj = torch.nn.Linear(64, 4 * 16, bias=False)   # 4 heads of 16
+        attn.k_proj = torch.nn.Linear(64, 2 * 16, bias=False)   # 2 KV heads (GQA groups of 2)
+        model.layers.append(attn)
+    return model.to(device=device, dtype=torch.bfloat16)
+
+
+def _qk_apply(device, maxima, process_group=None):
+    from muzo_clip_b200.qk_clip import QKClipController
+
+    model = _qk_model(device)
+    ctl = QKClipController(model, tau=10.0, alpha=0.5, process_group=process_group)
+    for name, vals in maxima.items():
+        ctl._captured_smax[name] = torch.tensor(vals, dtype=torch.float32, device=device)
+    stats = ctl.apply()
+    torch.cuda.synchronize()
+    return {n: p.detach().cpu() for n, p in model.named_parameters()}, stats
+
+
+def _qk_worker(rank: int, world: int, store: str, out_prefix: str) -> None:
+    sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
+    os.environ.update(NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    try:
+        weights, stats = _qk_apply(torch.device("cuda", rank), QK_MAXIMA[rank], dist.group.WORLD)
+        torch.save((weights, stats.qk_clip_count, stats.qk_smax_max), f"{out_prefix}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_qk_clip_with_per_rank_batches_matches_one_gpu(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    merged: dict[str, list[float]] = {}
+    for per_rank in QK_MAXIMA.values():
+        for name, vals in per_rank.items():
+            prev = merged.get(name, [float("-inf")] * len(vals))
+            merged[name] = [max(a, b) for a, b in zip(prev, vals)]
+    ref, ref_stats = _qk_apply(torch.device("cuda", 0), merged)
+    assert ref_stats.qk_clip_count > 0
+    mp.start_processes(_qk_worker, args=(2, str(tmp_path / "store"), str(tmp_path / "qk")), nprocs=2,
+                       start_method="spawn", join=True)
+    for r in range(2):
+        weights, count, smax = torch.load(tmp_path / f"qk.{r}")
+        assert (count, smax) == (ref_stats.qk_clip_count, ref_stats.qk_smax_max), r
+        for name, value in ref.items():
+            assert torch.equal(value, weights[name]), (r, name)
