@@ -457,7 +457,8 @@ class StepEngine:
         stats = host[self.stats_off: self.stats_off + 4 * _lib.NSTATS * n].view(np.float32).reshape(n, _lib.NSTATS)
         status = int(flags[n])
         if status != 0:
-            raise _lib.MuzoError(f"Newton-Schulz GEMM reported status {status} (bounded wait expired)")
+            raise _lib.MuzoError(f"Newton-Schulz GEMM reported status {status} (a bounded wait expired); the "
+                                 "weights this step updated are unspecified: restore them from a checkpoint")
         out: dict[int, dict[str, float]] = {}
         lr = np.float32(lr32)
         slot = 0
