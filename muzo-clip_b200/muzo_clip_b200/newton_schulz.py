@@ -161,9 +161,9 @@ def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int = 5) -> torch.Tensor
     device = src.device
     stream = _lib.stream_ptr(device)
     buf = allocate_ns_buffers(rows, cols, 1, device)
-    scratch = torch.zeros(_lib.NSUMS + 2, dtype=torch.float64, device=device)
+    scratch = torch.zeros(_lib.NSUMS + 3, dtype=torch.float64, device=device)
     sums_ptr = scratch.data_ptr()
-    flags = scratch[_lib.NSUMS:].view(torch.int32)  # [flag, status, ...]
+    flags = scratch[_lib.NSUMS:].view(torch.int32)  # [flag, the GEMMs' four status words, unused]
     flags_ptr = flags.data_ptr()
     status_ptr = flags_ptr + 4
 
