@@ -4,6 +4,7 @@ transformers calls during a probe forward, and the q/k row scaling."""
 from __future__ import annotations
 
 import contextvars
+import weakref
 
 import numpy as np
 import torch
@@ -49,9 +50,7 @@ def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: 
     and K [B, Hkv, Sk, D] (any strides with D contiguous)."""
     _check_cuda(query)
     if attention_mask is not None and not _is_plain_causal(attention_mask, query.shape[2], key.shape[2]):
-        # an additive mask that is not the plain causal mask: reduce explicit logits
-        from torch.nn import functional as F  # noqa: F401  (kept local: rare path)
-
+        # a mask that is not the plain causal mask (padding): reduce explicit logits
         group = query.shape[1] // key.shape[1]
         kr = key.repeat_interleave(group, dim=1)
         if attention_mask.dtype == torch.bool:
@@ -87,10 +86,31 @@ def eager_additive_mask(keep: torch.Tensor, causal: bool, dtype: torch.dtype) ->
     return torch.zeros(keep.shape, dtype=dtype, device=keep.device).masked_fill(~keep, torch.finfo(dtype).min)
 
 
+# mask object id -> (weak reference, (sq, sk, version), result): transformers builds one mask per
+# forward and hands the same tensor to every layer, so the test (two host syncs) runs once per
+# forward instead of once per layer
+_CAUSAL_CACHE: dict[int, tuple] = {}
+
+
 def _is_plain_causal(mask: torch.Tensor, sq: int, sk: int) -> bool:
     """True when a [B|1, 1|H, Sq, Sk] mask is the plain causal mask for every batch row: an
     additive mask 0 on and below the (end-aligned) diagonal and a large negative value above
-    it, or a boolean mask True exactly on and below it."""
+    it, or a boolean mask True exactly on and below it. Cached per mask tensor and version."""
+    try:
+        key = (int(sq), int(sk), mask._version)
+    except RuntimeError:  # inference tensors track no version: no caching
+        return _plain_causal_uncached(mask, sq, sk)
+    entry = _CAUSAL_CACHE.get(id(mask))
+    if entry is not None and entry[0]() is mask and entry[1] == key:
+        return entry[2]
+    result = _plain_causal_uncached(mask, sq, sk)
+    if len(_CAUSAL_CACHE) >= 64:
+        _CAUSAL_CACHE.clear()
+    _CAUSAL_CACHE[id(mask)] = (weakref.ref(mask), key, result)
+    return result
+
+
+def _plain_causal_uncached(mask: torch.Tensor, sq: int, sk: int) -> bool:
     if mask.ndim != 4 or mask.shape[-2] != sq or mask.shape[-1] != sk:
         return False
     i = torch.arange(sq, device=mask.device)[:, None] + (sk - sq)

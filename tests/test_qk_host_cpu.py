@@ -25,6 +25,27 @@ def test_plain_causal_detection_additive_and_boolean():
     assert not _is_plain_causal(additive[..., :8], 6, 9)   # shape mismatch
 
 
+def test_plain_causal_test_is_cached_per_mask_and_version(monkeypatch):
+    from muzo_clip_b200 import _qk
+
+    calls = []
+    real = _qk._plain_causal_uncached
+    monkeypatch.setattr(_qk, "_plain_causal_uncached", lambda *a: calls.append(1) or real(*a))
+    i = torch.arange(5)[:, None]
+    mask = torch.zeros(1, 1, 5, 5).masked_fill(torch.arange(5)[None, :] > i, torch.finfo(torch.float32).min)
+    for _ in range(4):  # one mask, every layer of a forward
+        assert _qk._is_plain_causal(mask, 5, 5)
+    assert len(calls) == 1
+    assert not _qk._is_plain_causal(mask, 5, 6) and len(calls) == 2   # other shape: computed
+    mask[0, 0, 4, 0] = torch.finfo(torch.float32).min                  # in place: new version
+    assert not _qk._is_plain_causal(mask, 5, 5) and len(calls) == 3
+    other = mask.clone()                                                # another tensor
+    assert not _qk._is_plain_causal(other, 5, 5) and len(calls) == 4
+    with torch.inference_mode():                                        # no version counter
+        inf_mask = torch.zeros(1, 1, 2, 2)
+    assert not _qk._is_plain_causal(inf_mask, 2, 2)
+
+
 def test_boolean_mask_to_eager_form_remasks_unmasked_padding_rows():
     from muzo_clip_b200._qk import eager_additive_mask
 
