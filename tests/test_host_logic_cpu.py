@@ -172,3 +172,73 @@ def test_state_dict_resumes_identically(monkeypatch):
     with pytest.raises(ValueError):
         c = mo.MuZOClipOptimizer(torch.nn.Linear(4, 4), **kw)
         c.load_state_dict(saved)
+
+
+def _public_members(module):
+    import inspect
+
+    return {n: o for n, o in vars(module).items()
+            if not n.startswith("_") and (inspect.isfunction(o) or inspect.isclass(o))
+            and getattr(o, "__module__", None) == module.__name__}
+
+
+def _assert_compatible(ref_fn, mine_fn, where: str) -> None:
+    """Every parameter of the reference callable exists here with the same kind and default;
+    parameters added here have defaults."""
+    import inspect
+
+    ref_sig, mine_sig = inspect.signature(ref_fn), inspect.signature(mine_fn)
+    for name, p in ref_sig.parameters.items():
+        assert name in mine_sig.parameters, f"{where}: parameter {name} missing"
+        q = mine_sig.parameters[name]
+        assert q.kind == p.kind, f"{where}: {name} is {q.kind}, reference {p.kind}"
+        assert q.default == p.default, f"{where}: default of {name}"
+    for name, q in mine_sig.parameters.items():
+        if name not in ref_sig.parameters:
+            assert q.default is not inspect.Parameter.empty or q.kind in (q.VAR_KEYWORD, q.VAR_POSITIONAL), \
+                f"{where}: added parameter {name} needs a default"
+
+
+@pytest.mark.skipif(not _have_reference(), reason="reference package not mounted")
+def test_public_api_matches_reference():
+    """The drop-in contract: every public function, class, method, property and dataclass field
+    of the reference's modules exists here with compatible parameters and the same defaults."""
+    import dataclasses
+    import importlib
+    import inspect
+
+    sys.path.insert(0, REF)
+    try:
+        ref_pkg = importlib.import_module("muzo_clip")
+        mine_pkg = importlib.import_module("muzo_clip_b200")
+        assert set(ref_pkg.__all__) <= set(mine_pkg.__all__)
+        checked = 0
+        for mod in ("muzo_optimizer", "newton_schulz", "parameter_filter", "prng", "qk_clip", "integration"):
+            ref_mod = importlib.import_module(f"muzo_clip.{mod}")
+            mine_mod = importlib.import_module(f"muzo_clip_b200.{mod}")
+            for name, ref_obj in _public_members(ref_mod).items():
+                mine_obj = getattr(mine_mod, name, None)
+                assert mine_obj is not None, f"{mod}.{name} missing"
+                if inspect.isfunction(ref_obj):
+                    _assert_compatible(ref_obj, mine_obj, f"{mod}.{name}")
+                    checked += 1
+                    continue
+                if dataclasses.is_dataclass(ref_obj):
+                    assert [f.name for f in dataclasses.fields(ref_obj)] == \
+                        [f.name for f in dataclasses.fields(mine_obj)], f"{mod}.{name} fields"
+                    checked += 1
+                    continue
+                _assert_compatible(ref_obj.__init__, mine_obj.__init__, f"{mod}.{name}.__init__")
+                for attr, member in vars(ref_obj).items():
+                    if attr.startswith("_"):
+                        continue
+                    mine_member = inspect.getattr_static(mine_obj, attr, None)
+                    assert mine_member is not None, f"{mod}.{name}.{attr} missing"
+                    if isinstance(member, property):
+                        assert isinstance(mine_member, property), f"{mod}.{name}.{attr} is not a property"
+                    elif inspect.isfunction(member):
+                        _assert_compatible(member, getattr(mine_obj, attr), f"{mod}.{name}.{attr}")
+                    checked += 1
+        assert checked >= 25  # the loops above did run over the whole surface
+    finally:
+        sys.path.remove(REF)
