@@ -181,6 +181,8 @@ int muzo_qk_max(const void* q, const void* k, int dtype, int64_t batch, int64_t 
   if (q == nullptr || k == nullptr || smax == nullptr || d_valid == nullptr || batch < 0 || hq <= 0 ||
       hkv <= 0 || hq % hkv != 0 || seq_q < 0 || seq_k < 0 || head_dim <= 0)
     return MUZO_ERR_ARG;
+  if (dtype != MUZO_BF16 && dtype != MUZO_F16 && dtype != MUZO_F32) return MUZO_ERR_DTYPE;  // before any launch
+  if (hq > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* enc = reinterpret_cast<int*>(smax);
   init_max_kernel<<<static_cast<unsigned>((hq + 255) / 256), 256, 0, s>>>(enc, static_cast<int>(hq), d_valid);
@@ -234,6 +236,7 @@ int muzo_logits_head_max(const void* logits, int dtype, int64_t batch, int64_t h
   if (logits == nullptr || out == nullptr || d_valid == nullptr || batch < 0 || heads <= 0 || seq_q < 0 ||
       seq_k < 0 || heads > 65535)
     return MUZO_ERR_ARG;
+  if (dtype != MUZO_BF16 && dtype != MUZO_F16 && dtype != MUZO_F32) return MUZO_ERR_DTYPE;  // before any launch
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* enc = reinterpret_cast<int*>(out);
   init_max_kernel<<<static_cast<unsigned>((heads + 255) / 256), 256, 0, s>>>(enc, static_cast<int>(heads), d_valid);
@@ -270,6 +273,7 @@ int muzo_logits_head_max(const void* logits, int dtype, int64_t batch, int64_t h
 int muzo_max_merge(float* running, const float* fresh, const int32_t* d_valid, int64_t n, void* stream) {
   if (running == nullptr || fresh == nullptr || n < 0) return MUZO_ERR_ARG;
   if (n == 0) return MUZO_OK;
+  if (n > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;
   max_merge_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       running, fresh, d_valid, static_cast<int>(n));
   return launch_status();

@@ -118,3 +118,58 @@ def test_status_strings_and_bad_args():
     assert _lib.lib.muzo_ns_gemm(None, 8, 0, 0, None, 8, 0, 0, None, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None) == 1
     # unaligned leading dimension
     assert _lib.lib.muzo_ns_gemm(16, 12, 0, 0, 16, 8, 0, 0, 16, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None) == 3
+
+
+# A fake, never-dereferenced device address: every call below is rejected by the library's host
+# checks before anything is launched (safe with or without a GPU).
+_P = 256
+
+
+@pytest.mark.parametrize("call, expected", [
+    # noise and perturbation: table, keys, enums, item counts
+    (lambda L: L.muzo_fill_noise(None, 1, 1024, 1, 0, 1, None), 1),
+    (lambda L: L.muzo_fill_noise(_P, 1, 1000, 1, 0, 1, None), 1),          # not whole CTAs
+    (lambda L: L.muzo_fill_noise(_P, 1, 1024, 1, 0, 9, None), 2),          # dtype
+    (lambda L: L.muzo_fill_noise(_P, 1, 1024, 1, 7, 1, None), 1),          # distribution
+    (lambda L: L.muzo_perturb_segments(_P, 1, 1024, None, 1, 0, 1.0, None), 1),
+    (lambda L: L.muzo_perturb_segments(_P, 1, 1024, _P, 1, 5, 1.0, None), 1),
+    (lambda L: L.muzo_perturb_segments(_P, 1, 1024, _P, 9, 0, 1.0, None), 2),
+    (lambda L: L.muzo_perturb_segments(None, 0, 0, None, 9, 0, 1.0, None), 0),   # empty: no-op
+    (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 0, 0, 1, 1, 1.0, _P, _P, 0, None), 1),  # horizon
+    (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 1, 1, 1.0, None, _P, 0, None), 1),
+    (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 9, 1, 1.0, _P, _P, 0, None), 2),
+    # element-wise step kernels
+    (lambda L: L.muzo_ns_prepare(_P, 1, 1024, 1, None, _P, None), 1),
+    (lambda L: L.muzo_ns_prepare(_P, 1, 1024, 9, _P, _P, None), 2),
+    (lambda L: L.muzo_ns_normalize(None, 1, 1024, _P, _P, None), 1),
+    (lambda L: L.muzo_ns_normalize(_P, 1, 1024, _P, None, None), 1),
+    (lambda L: L.muzo_update_sumsq(_P, 1, 1024, None, _P, _P, None), 1),
+    (lambda L: L.muzo_apply_update(_P, 1, 1024, 1, _P, 1e-3, 0.01, 1, 1.0, _P, _P, None, None), 1),
+    (lambda L: L.muzo_apply_update(_P, 1, 1024, 9, _P, 1e-3, 0.01, 1, 1.0, _P, _P, _P, None), 2),
+    (lambda L: L.muzo_ns_normalize_noalloc(None, None, None, 65, 1, _P, None), 1),
+    (lambda L: L.muzo_ns_normalize_noalloc((ctypes.c_void_p * 65)(), (ctypes.c_void_p * 65)(),
+                                           (ctypes.c_int64 * 65)(), 65, 1, _P, None), 5),  # capacity
+    (lambda L: L.muzo_ns_normalize_noalloc((ctypes.c_void_p * 1)(), (ctypes.c_void_p * 1)(),
+                                           (ctypes.c_int64 * 1)(), 1, 9, _P, None), 2),
+    # Newton-Schulz GEMM: epilogue operand, epilogue code, symmetric shapes, leading dimensions
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 1, 1.0, 1.0, 8, 8, 8, 1, 0, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 3, 1.0, 1.0, 8, 8, 8, 1, 0, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 16, 0, None, 0, 0.0, 0.0, 8, 16, 8, 1, 1, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 2, 1.0, 0.0, 8, 8, 8, 1, 1, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 16, 1, 0, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P + 8, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None), 3),
+    # QK-Clip
+    (lambda L: L.muzo_qk_max(None, _P, 1, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 1),
+    (lambda L: L.muzo_qk_max(_P, _P, 1, 1, 8, 3, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 1),  # GQA
+    (lambda L: L.muzo_qk_max(_P, _P, 9, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 2),
+    (lambda L: L.muzo_logits_head_max(_P, 1, 1, 70000, 4, 4, 0, 0, 0, 0, _P, _P, None), 1),
+    (lambda L: L.muzo_logits_head_max(_P, 9, 1, 8, 4, 4, 0, 0, 0, 0, _P, _P, None), 2),
+    (lambda L: L.muzo_max_merge(_P, _P, None, -1, None), 1),
+    (lambda L: L.muzo_max_merge(_P, _P, None, 0, None), 0),                 # empty: no-op
+    (lambda L: L.muzo_qk_scale_rows(None, 1, 2, 2, 2, _P, _P, None), 1),
+    (lambda L: L.muzo_qk_scale_rows(_P, 1, 2, 2, 2, _P, None, None), 1),
+])
+def test_entry_points_reject_bad_arguments_before_any_launch(call, expected):
+    from muzo_clip_b200 import _lib
+
+    assert call(_lib.lib) == expected
