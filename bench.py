@@ -230,7 +230,7 @@ def run_gpu(args) -> int:
     model = Llama8BMatrices(device, layers=args.layers)
     pg = dist.group.WORLD if dist is not None else None
     opt = MuZOClipOptimizer(model, horizon=HORIZON, min_history=4, beta_momentum=0.9, lr=1e-5, seed=1234,
-                            process_group=pg)
+                            process_group=pg, noise_cache=args.noise_cache)
     rng = random.Random(99)
     for _ in range(HORIZON):
         opt.history.append(HistoryItem(rng.randrange(0, 2**63 - 1), max(-3.0, min(3.0, rng.gauss(0, 1))), 0.0, 0.0, 0.0))
@@ -331,6 +331,7 @@ def run_gpu(args) -> int:
             "config": {"workload": WORKLOAD, "layers": args.layers, "matrices": len(engine.blocks),
                        "elements": n_elems, "horizon": HORIZON, "ns_steps": 5, "distribution": "normal",
                        "parallelism": f"replica perturb + NS partition x{world}",
+                       "noise_cache": bool(engine.keep_noise),
                        "l2": "inputs larger than L2 (14 GB of weights per pass)"},
             "perturb_gbs": round(perturb_gbs, 1),
             "perturb_ms": round(perturb_ms, 3),
@@ -580,6 +581,8 @@ def main() -> int:
     ap.add_argument("--impl", default="muzo", choices=["muzo", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--noise-cache", action="store_true",
+                    help="keep each projection's noise between its passes (MuZOClipOptimizer(noise_cache=True))")
     ap.add_argument("--sweep", action="store_true",
                     help="with --case: ns = 5 shapes x batch 8; perturb = 1 M..2 G elements; rebuild = horizon 1..16")
     args = ap.parse_args()

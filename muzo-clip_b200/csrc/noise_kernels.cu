@@ -173,13 +173,18 @@ struct Packed8 {
   }
 };
 
-template <int DIST, int DTYPE>
+// KEEP (normal noise only): also store the rounded noise dtype(Z) of every element to segs[i].out,
+// laid out like the block, so that the other passes of the same projection can read it back
+// instead of regenerating it.
+template <int DIST, int DTYPE, bool KEEP = false>
 __global__ void __launch_bounds__(kElemThreads, 4)
 perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
                float alpha) {
+  static_assert(!KEEP || DIST == MUZO_NORMAL, "only normal noise is kept");
   const SegView sv = cta_segment(segs, nsegs, DTYPE, DTYPE);
   const uint32_t octets = sv.threads / 8;
-  const bool vec = vec_ok(sv.param, 0, DTYPE);
+  const bool keep = KEEP && sv.out != nullptr;  // a segment without a noise buffer only perturbs
+  const bool vec = vec_ok(sv.param, 0, DTYPE) && (!keep || vec_ok(sv.out, 0, DTYPE));
   const uint64_t key = keys[sv.block];
 #pragma unroll 1
   for (int it = 0; it < kItemsPerThread; ++it) {
@@ -242,6 +247,7 @@ perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
           load8(sv.param, li, DTYPE, w);
 #pragma unroll
           for (int k = 0; k < 8; k += 2) round2_to(z[j][k], z[j][k + 1], DTYPE);
+          if (keep) store8(sv.out, li, DTYPE, z[j]);  // exact: z is already rounded to DTYPE
 #pragma unroll
           for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, z[j][k], w[k]);
           store8(sv.param, li, DTYPE, w);
@@ -250,7 +256,9 @@ perturb_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
           for (int k = 0; k < 8; ++k) {  // static indices keep z in registers
             if (li + k < sv.numel) {
               const float w = load_elem(sv.param, li + k, DTYPE);
-              store_elem(sv.param, li + k, DTYPE, __fmaf_rn(alpha, round_to(z[j][k], DTYPE), w));
+              const float zr = round_to(z[j][k], DTYPE);
+              if (keep) store_elem(sv.out, li + k, DTYPE, zr);
+              store_elem(sv.param, li + k, DTYPE, __fmaf_rn(alpha, zr, w));
             }
           }
         }
@@ -473,6 +481,22 @@ int muzo_perturb_segments(const muzo_segment* d_segs, int nsegs, int64_t total_i
       perturb_kernel<MUZO_NORMAL, D><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_keys, alpha);
     else
       perturb_kernel<MUZO_RADEMACHER, D><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_keys, alpha);
+  });
+  if (st != MUZO_OK) return st;
+  return launch_status();
+}
+
+int muzo_perturb_segments_keep_noise(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                                     const uint64_t* d_keys, int dtype, float alpha, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_table(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_keys == nullptr) return MUZO_ERR_ARG;
+  const dim3 grid(static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dispatch_dtype(dtype, [&](auto d) {
+    constexpr int D = decltype(d)::value;
+    perturb_kernel<MUZO_NORMAL, D, true><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_keys, alpha);
   });
   if (st != MUZO_OK) return st;
   return launch_status();

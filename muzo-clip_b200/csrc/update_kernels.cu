@@ -165,6 +165,39 @@ update_sumsq_kernel(const muzo_segment* __restrict__ segs, int nsegs, const floa
   if (!finite) atomicOr(flags + v.block, MUZO_FLAG_NONFINITE_OUTPUT);
 }
 
+// ------------------------------------------------------------------ perturbation from kept noise
+// W <- dtype(W + alpha * Zk) with Zk (segs[i].out, the block's dtype and layout) the rounded noise
+// a normal-noise pass of the same key kept: the arithmetic of the regenerating pass
+// (add_(noise, alpha) as one fp32 fused multiply-add, then the rounding to the weight dtype) on
+// values read from memory, 6 B per 16-bit element instead of a Philox + Box-Muller evaluation.
+template <int DTYPE>
+__global__ void __launch_bounds__(kElemThreads)
+perturb_kept_kernel(const muzo_segment* __restrict__ segs, int nsegs, float alpha) {
+  const LinView v = cta_linear(segs, nsegs);
+  if (v.param == nullptr || v.out == nullptr) return;
+  const bool vec = aligned16(v.param) && aligned16(v.out);
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const int64_t item = v.local_item0 + it * kElemThreads + threadIdx.x;
+    const int64_t li = item * 8;
+    if (li >= v.numel) break;
+    if (vec && li + 8 <= v.numel) {
+      float w[8], z[8];
+      load8(v.out, li, DTYPE, z);
+      load8(v.param, li, DTYPE, w);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(alpha, z[k], w[k]);
+      store8(v.param, li, DTYPE, w);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (li + k < v.numel)
+          store_elem(v.param, li + k, DTYPE,
+                     __fmaf_rn(alpha, load_elem(v.out, li + k, DTYPE), load_elem(v.param, li + k, DTYPE)));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ apply
 struct ApplyScalars {
   float clip;     // multiplier applied to U
@@ -312,6 +345,22 @@ int muzo_update_sumsq(const muzo_segment* d_segs, int nsegs, int64_t total_items
   if (d_scales == nullptr || d_sums == nullptr || d_flags == nullptr) return MUZO_ERR_ARG;
   update_sumsq_kernel<<<static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA), kElemThreads, 0,
                         static_cast<cudaStream_t>(stream)>>>(d_segs, nsegs, d_scales, d_sums, d_flags);
+  return launch_status();
+}
+
+int muzo_perturb_kept_noise(const muzo_segment* d_segs, int nsegs, int64_t total_items, int dtype,
+                            float alpha, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_linear(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  const unsigned grid = static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case MUZO_BF16: perturb_kept_kernel<MUZO_BF16><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, alpha); break;
+    case MUZO_F16: perturb_kept_kernel<MUZO_F16><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, alpha); break;
+    case MUZO_F32: perturb_kept_kernel<MUZO_F32><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, alpha); break;
+    default: return MUZO_ERR_DTYPE;
+  }
   return launch_status();
 }
 

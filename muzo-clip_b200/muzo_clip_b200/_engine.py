@@ -9,6 +9,7 @@ apply, and the step statistics come back in one device-to-host copy.
 
 from __future__ import annotations
 
+import logging
 import math
 import os
 from dataclasses import dataclass, field
@@ -22,6 +23,8 @@ from .newton_schulz import NSBuffers, ns_buffers_in, ns_iterations, ns_workspace
 from .prng import hash64_seed, iter_param_blocks
 
 DEFAULT_WORKSPACE_BYTES = 16 << 30
+
+logger = logging.getLogger(__name__)
 
 
 @dataclass
@@ -49,6 +52,15 @@ class PerturbGroup:
     table: torch.Tensor
     nsegs: int
     total_items: int
+    # kept noise: the first pass of a seed stores dtype(Z) (keep_*: noise segments whose out is
+    # the block's slot of the noise buffer), later passes of that seed read it back (kept_*:
+    # linear segments, param = block, out = its noise)
+    keep_table: torch.Tensor | None = None
+    keep_nsegs: int = 0
+    keep_items: int = 0
+    kept_table: torch.Tensor | None = None
+    kept_nsegs: int = 0
+    kept_items: int = 0
 
 
 @dataclass
@@ -140,6 +152,11 @@ class StepEngine:
         self.dist = _lib.dist_code(opt.distribution)
         self.sms, self.max_thr = _lib.device_geometry(self.device)
         self._key_cache: dict[int, np.ndarray] = {}
+        # noise kept between the passes of one projection (normal noise only: Rademacher passes
+        # are already close to the HBM rate)
+        self.keep_noise = bool(getattr(opt, "noise_cache", False)) and self.dist == _lib.NORMAL
+        self.noise_buffer: torch.Tensor | None = None
+        self._kept_seed: int | None = None
         self._build_perturb_groups()
         costs = [ns_flops(b.rows, b.cols, max(opt.ns_steps, 1)) for b in blocks]
         self.owner = partition_blocks(costs, world) if world > 1 else [0] * len(blocks)
@@ -156,7 +173,8 @@ class StepEngine:
     @staticmethod
     def _fingerprint(opt) -> tuple:
         return tuple((s.name, s.param.data.data_ptr(), tuple(s.param.shape), s.param.dtype)
-                     for s in opt.selected_params) + (opt.block_rows, opt.distribution)
+                     for s in opt.selected_params) + (opt.block_rows, opt.distribution,
+                                                      bool(getattr(opt, "noise_cache", False)))
 
     def matches(self, opt) -> bool:
         return self.fingerprint == self._fingerprint(opt)
@@ -182,25 +200,68 @@ class StepEngine:
             # block_index in the table indexes the group's key array
             table = _lib.to_device_table(segs, self.device)
             self.perturb_groups.append(PerturbGroup(code, blks, table, len(segs), total))
+        if self.keep_noise:
+            self._build_noise_buffer()
+
+    def _build_noise_buffer(self) -> None:
+        """One device buffer for the rounded noise of every block (the block's dtype and layout,
+        256-byte aligned slots) and the two tables per group that write and read it. Left out,
+        with a warning, when it would take more than half of the free device memory."""
+        offsets, total = [], 0
+        for b in self.blocks:
+            offsets.append(total)
+            total += (b.numel * b.tensor.element_size() + 255) // 256 * 256
+        free, _ = torch.cuda.mem_get_info(self.device)
+        if total > free // 2:
+            logger.warning("noise_cache needs %.1f GB of device memory, more than half of the %.1f GB free; "
+                           "every pass regenerates its noise instead", total / 1e9, free / 1e9)
+            self.keep_noise = False
+            return
+        self.noise_buffer = torch.empty(max(total, 256), dtype=torch.uint8, device=self.device)
+        base = self.noise_buffer.data_ptr()
+        for g in self.perturb_groups:
+            numels = [b.numel for b in g.blocks]
+            params = [b.tensor.data_ptr() for b in g.blocks]
+            outs = [base + offsets[b.index] for b in g.blocks]
+            segs, items = _lib.plan_segments(numels, params, outs, self.dist, self.sms, self.max_thr)
+            g.keep_table, g.keep_nsegs, g.keep_items = _lib.to_device_table(segs, self.device), len(segs), items
+            lsegs, litems = _lib.plan_linear(numels, params, outs)
+            g.kept_table, g.kept_nsegs, g.kept_items = _lib.to_device_table(lsegs, self.device), len(lsegs), litems
 
     def perturb(self, seed: int, alpha: float) -> None:
-        """W <- W + alpha * Z(seed) for every selected block (muzo_optimizer.py:434-446)."""
+        """W <- W + alpha * Z(seed) for every selected block (muzo_optimizer.py:434-446). With the
+        noise buffer, the first pass of a seed also keeps dtype(Z) and the following passes of the
+        same seed read it back: the same values without regenerating the noise."""
         if not self.blocks:
             return
-        keys = self.keys_for(seed)
         stream = _lib.stream_ptr(self.device)
-        dev_keys = self.uploader.upload(keys)
-        self._mark("perturb", True)
         alpha32 = float(np.float32(alpha))
+        if self.keep_noise and self._kept_seed == seed:
+            self._mark("perturb", True)
+            for g in self.perturb_groups:
+                _lib.launch("muzo_perturb_kept_noise", g.kept_table.data_ptr(), g.kept_nsegs, g.kept_items,
+                            g.dtype_code, alpha32, stream)
+            self._mark("perturb", False)
+            return
+        keys = self.keys_for(seed)
+        dev_keys = self.uploader.upload(keys)
+        self._kept_seed = None  # the buffer is being rewritten
+        self._mark("perturb", True)
         for g in self.perturb_groups:
             idx = np.fromiter((b.index for b in g.blocks), dtype=np.int64, count=len(g.blocks))
             if len(self.perturb_groups) == 1 and np.array_equal(idx, np.arange(len(self.blocks))):
                 kptr = dev_keys.data_ptr()
             else:
                 kptr = self.uploader.upload(keys[idx]).data_ptr()
-            _lib.launch("muzo_perturb_segments", g.table.data_ptr(), g.nsegs, g.total_items, kptr, g.dtype_code,
-                        self.dist, alpha32, stream)
+            if self.keep_noise:
+                _lib.launch("muzo_perturb_segments_keep_noise", g.keep_table.data_ptr(), g.keep_nsegs,
+                            g.keep_items, kptr, g.dtype_code, alpha32, stream)
+            else:
+                _lib.launch("muzo_perturb_segments", g.table.data_ptr(), g.nsegs, g.total_items, kptr,
+                            g.dtype_code, self.dist, alpha32, stream)
         self._mark("perturb", False)
+        if self.keep_noise:
+            self._kept_seed = seed
 
     # ------------------------------------------------------------------ step
     def _workspace_budget(self) -> int:

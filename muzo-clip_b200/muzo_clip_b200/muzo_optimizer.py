@@ -5,11 +5,14 @@ Same constructor, methods, validation errors, skip logic and returned dicts as t
 model-sized work — perturbation, momentum rebuild, Newton-Schulz and the update — runs in the
 native library through ``_engine.StepEngine``.
 
-Two keyword arguments are additions: ``process_group`` shards the step over the ranks of a
+Three keyword arguments are additions: ``process_group`` shards the step over the ranks of a
 torch.distributed group (each rank rebuilds, orthogonalises and applies the blocks it owns, and
 NCCL broadcasts the updated weights; SPSA losses are averaged over the group and QK-Clip maxima
-max-reduced, so ranks may feed different batches), and
-``workspace_bytes`` bounds the Newton-Schulz workspace.
+max-reduced, so ranks may feed different batches),
+``workspace_bytes`` bounds the Newton-Schulz workspace, and ``noise_cache=True`` keeps the
+rounded normal noise of the current projection on the device (one buffer the size of the
+selected weights, left out when it would take more than half of the free memory) so that its
+-2eps and +eps passes read it back instead of regenerating it; results are bit-identical.
 """
 
 from __future__ import annotations
@@ -111,6 +114,7 @@ class MuZOClipOptimizer:
         qk_clip_alpha: float = 0.5,
         process_group=None,
         workspace_bytes: int | None = None,
+        noise_cache: bool = False,
     ):
         # argument validation of muzo_optimizer.py:109-122, same messages
         checks = (
@@ -148,6 +152,7 @@ class MuZOClipOptimizer:
         self.qk_capture_clean_forward = bool(qk_capture_clean_forward)
         self.workspace_bytes = workspace_bytes
         self.process_group = process_group
+        self.noise_cache = bool(noise_cache)
 
         self.selected_params: list[SelectedParameter] = select_muzo_parameters(
             model, trainable_substrings=trainable_substrings, frozen_substrings=frozen_substrings

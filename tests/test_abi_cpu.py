@@ -135,6 +135,13 @@ _P = 256
     (lambda L: L.muzo_perturb_segments(_P, 1, 1024, _P, 1, 5, 1.0, None), 1),
     (lambda L: L.muzo_perturb_segments(_P, 1, 1024, _P, 9, 0, 1.0, None), 2),
     (lambda L: L.muzo_perturb_segments(None, 0, 0, None, 9, 0, 1.0, None), 0),   # empty: no-op
+    (lambda L: L.muzo_perturb_segments_keep_noise(None, 1, 1024, _P, 1, 1.0, None), 1),
+    (lambda L: L.muzo_perturb_segments_keep_noise(_P, 1, 1024, None, 1, 1.0, None), 1),
+    (lambda L: L.muzo_perturb_segments_keep_noise(_P, 1, 1024, _P, 9, 1.0, None), 2),
+    (lambda L: L.muzo_perturb_kept_noise(None, 1, 1024, 1, 1.0, None), 1),
+    (lambda L: L.muzo_perturb_kept_noise(_P, 1, 1000, 1, 1.0, None), 1),
+    (lambda L: L.muzo_perturb_kept_noise(_P, 1, 1024, 9, 1.0, None), 2),
+    (lambda L: L.muzo_perturb_kept_noise(None, 0, 0, 9, 1.0, None), 0),          # empty: no-op
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 0, 0, 1, 1, 1.0, _P, _P, 0, None), 1),  # horizon
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 1, 1, 1.0, None, _P, 0, None), 1),
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 9, 1, 1.0, _P, _P, 0, None), 2),

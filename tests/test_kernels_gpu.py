@@ -99,6 +99,86 @@ def test_perturb_bit_exact(device, dist, dtype, block_rows):
             assert torch.equal(p1, p2), (n1, seed, s)
 
 
+class _MixedMats(torch.nn.Module):
+    """Blocks of two dtypes (two perturbation groups), ragged sizes included."""
+
+    def __init__(self, device):
+        super().__init__()
+        self.a = _Mats([(64, 128), (200, 72), (7, 9)], torch.bfloat16, device, seed=1)
+        self.b = _Mats([(96, 40), (33, 31)], torch.float32, device, seed=2)
+        self.c = _Mats([(128, 64)], torch.float16, device, seed=3)
+
+
+@pytest.mark.parametrize("block_rows", [None, 48])
+def test_perturb_with_kept_noise_bit_exact(device, block_rows):
+    """noise_cache=True: the first pass of a seed keeps dtype(Z), later passes of that seed read
+    it back; every pass must equal the reference path's regenerated noise, and the kept noise
+    must equal the noise itself."""
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = _MixedMats(device)
+    twin = copy.deepcopy(model)
+    opt = MuZOClipOptimizer(model, distribution="normal", block_rows=block_rows, noise_cache=True)
+    named = [(n, p) for n, p in twin.named_parameters() if n in set(opt.selected_parameter_names())]
+    eng = opt._engine_for_step()
+    assert eng.keep_noise and eng.noise_buffer is not None and len(eng.perturb_groups) == 3
+    # keep, two reads, a new seed (rewrite), reads, an earlier seed again (rewrite)
+    for seed, s in ((11, 1.0), (11, -2.0), (11, 1.0), (12, 1.0), (12, -2.0), (12, 1.0), (11, -1.0)):
+        opt._perturb_selected(seed, s)
+        tr.perturb(named, seed, s, opt.zo_eps, "normal", block_rows)
+        for (n1, p1), (_, p2) in zip(model.named_parameters(), twin.named_parameters()):
+            assert torch.equal(p1, p2), (n1, seed, s)
+    assert eng._kept_seed == 11
+    torch.cuda.synchronize()
+    # the kept noise of every block is dtype(randn) of its key
+    off = 0
+    for b in eng.blocks:
+        nbytes = b.numel * b.tensor.element_size()
+        kept = eng.noise_buffer[off:off + nbytes].view(b.dtype).view(b.rows, b.cols)
+        ref = tr.noise_like(b.tensor, 11, b.name, b.block_index, "normal")
+        assert torch.equal(kept, ref), b.name
+        off += (nbytes + 255) // 256 * 256
+
+
+def test_steps_with_noise_cache_match_steps_without(device):
+    """Projections and steps through the public API: bit-identical weights, projections and step
+    statistics with and without the kept noise."""
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = _MixedMats(device)
+    twin = copy.deepcopy(model)
+    kw = dict(seed=9, horizon=3, min_history=1, lr=1e-3)
+    cached = MuZOClipOptimizer(model, noise_cache=True, **kw)
+    plain = MuZOClipOptimizer(twin, **kw)
+
+    def loss(m):
+        return float(m.a.layers[0].q_proj.weight.float().square().sum().item())
+
+    for _ in range(4):
+        assert cached.estimate_projection(lambda: loss(model)) == plain.estimate_projection(lambda: loss(twin))
+        assert cached.step() == plain.step()
+        for (n1, p1), (_, p2) in zip(model.named_parameters(), twin.named_parameters()):
+            assert torch.equal(p1, p2), n1
+
+
+def test_noise_cache_left_out_without_room(device, monkeypatch, caplog):
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = _Mats([(64, 128)], torch.bfloat16, device)
+    monkeypatch.setattr(torch.cuda, "mem_get_info", lambda *a: (1024, 1 << 40))
+    opt = MuZOClipOptimizer(model, noise_cache=True)
+    with caplog.at_level("WARNING"):
+        eng = opt._engine_for_step()
+    assert not eng.keep_noise and eng.noise_buffer is None
+    assert any("noise_cache" in r.message for r in caplog.records)
+    twin = copy.deepcopy(model)
+    ref = MuZOClipOptimizer(twin)
+    for seed, s in ((5, 1.0), (5, -2.0)):
+        opt._perturb_selected(seed, s)
+        ref._perturb_selected(seed, s)
+    assert torch.equal(model.layers[0].q_proj.weight, twin.layers[0].q_proj.weight)
+
+
 # ---------------------------------------------------------------- rebuild
 
 
