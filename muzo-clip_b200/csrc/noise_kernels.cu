@@ -83,6 +83,7 @@ __device__ __forceinline__ bool vec_ok(const void* base, int64_t elem_start, int
 struct SegView {
   char* param;
   char* out;
+  char* kept;           // the block's kept noise (parameter dtype), or NULL
   int64_t numel;
   int64_t local_item0;  // first item of this CTA relative to the segment
   uint64_t philox_offset;
@@ -99,6 +100,7 @@ __device__ __forceinline__ SegView cta_segment(const muzo_segment* segs, int nse
   SegView v;
   v.param = g.param ? static_cast<char*>(g.param) + g.elem_start * elem_size(pdtype) : nullptr;
   v.out = g.out ? static_cast<char*>(g.out) + g.elem_start * elem_size(odtype) : nullptr;
+  v.kept = g.kept ? static_cast<char*>(g.kept) + g.elem_start * elem_size(pdtype) : nullptr;
   v.numel = g.numel;
   v.local_item0 = item0 - g.item_begin;
   v.philox_offset = g.philox_offset;
@@ -335,6 +337,27 @@ __device__ __forceinline__ void load4(const void* base, int64_t i, int dtype, fl
   }
 }
 
+// acc[j][k] += alpha * zk for the kept noise zk (already dtype(Z)) of elements li0 + S*j + k:
+// the arithmetic of accumulate4x4's normal branch on values read from memory.
+template <int PDTYPE>
+__device__ __forceinline__ void accumulate_kept4x4(const char* kept, int64_t li0, uint32_t threads, int64_t numel,
+                                                   bool vec, float alpha, float (&acc)[4][4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t li = li0 + static_cast<int64_t>(threads) * j;
+    if (li >= numel) break;
+    float z[4];
+    if (vec && li + 4 <= numel) {
+      load4(kept, li, PDTYPE, z);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) z[k] = li + k < numel ? load_elem(kept, li + k, PDTYPE) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[j][k] = __fmaf_rn(alpha, z[k], acc[j][k]);
+  }
+}
+
 __device__ __forceinline__ void store4_bf16(void* base, int64_t i, const float (&v)[4]) {
   uint2 u;
   u.x = pack_bf16(v[0], v[1]);
@@ -344,7 +367,8 @@ __device__ __forceinline__ void store4_bf16(void* base, int64_t i, const float (
 
 // M = sum_h alphas[h] * float(dtype(Z_h)) (h = age, newest first, as the reference walks
 // reversed(history)); M *= inv_coeff_sum; out = bf16(M). Also sums M^2, bf16(M)^2 and W^2.
-template <int DIST, int PDTYPE>
+// KEPT: Z_0 is read from the segment's kept noise (when it has one) instead of regenerated.
+template <int DIST, int PDTYPE, bool KEPT = false>
 __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ segs, int nsegs,
                                               const uint64_t* __restrict__ keys, const float* __restrict__ alphas,
                                               int horizon, int normalize, float inv_coeff_sum,
@@ -353,6 +377,9 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
   const SegView sv = cta_segment(segs, nsegs, PDTYPE, MUZO_BF16, chunk);
   const uint32_t octets = sv.threads / 8;
   const bool vec = vec_ok(sv.out, 0, MUZO_BF16) && vec_ok(sv.param, 0, PDTYPE);
+  const bool use_kept = KEPT && sv.kept != nullptr;
+  const bool kept_vec = use_kept && vec_ok(sv.kept, 0, PDTYPE);
+  const int h_first = use_kept ? 1 : 0;
   const uint64_t* bkeys = keys + static_cast<int64_t>(sv.block) * horizon;
   const int half = threadIdx.x & 1;          // which quad of the item's eight launch threads
   const int slot = threadIdx.x >> 1;         // item slot within the CTA's 256-item stride
@@ -370,8 +397,9 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
     for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int k = 0; k < 4; ++k) acc[j][k] = 0.0f;
+    if (use_kept) accumulate_kept4x4<PDTYPE>(sv.kept, li0, sv.threads, sv.numel, kept_vec, alphas[0], acc);
 #pragma unroll 1
-    for (int h = 0; h < horizon; ++h)
+    for (int h = h_first; h < horizon; ++h)
       accumulate4x4<DIST, PDTYPE>(bkeys[h], 8ull * oct + 4 * half, sv.philox_offset, trip, alphas[h], acc);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -413,7 +441,7 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
   if (!finite) atomicOr(flags + sv.block, MUZO_FLAG_NONFINITE_INPUT);
 }
 
-template <int DIST, int PDTYPE>
+template <int DIST, int PDTYPE, bool KEPT = false>
 __global__ void __launch_bounds__(kRebuildThreads, 2)
 rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
                const float* __restrict__ alphas, int horizon, int normalize, float inv_coeff_sum,
@@ -421,7 +449,8 @@ rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t*
   // a CTA walks chunks blockIdx.x, blockIdx.x + gridDim.x, ... (grid may be smaller than the
   // number of chunks, e.g. one CTA per SM next to a concurrently running GEMM)
   for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x)
-    rebuild_chunk<DIST, PDTYPE>(segs, nsegs, keys, alphas, horizon, normalize, inv_coeff_sum, sums, flags, chunk);
+    rebuild_chunk<DIST, PDTYPE, KEPT>(segs, nsegs, keys, alphas, horizon, normalize, inv_coeff_sum, sums, flags,
+                                      chunk);
 }
 
 bool valid_dtype(int d) { return d == MUZO_F32 || d == MUZO_BF16 || d == MUZO_F16; }
@@ -497,6 +526,28 @@ int muzo_perturb_segments_keep_noise(const muzo_segment* d_segs, int nsegs, int6
   st = dispatch_dtype(dtype, [&](auto d) {
     constexpr int D = decltype(d)::value;
     perturb_kernel<MUZO_NORMAL, D, true><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_keys, alpha);
+  });
+  if (st != MUZO_OK) return st;
+  return launch_status();
+}
+
+int muzo_rebuild_segments_kept(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                               const uint64_t* d_keys, const float* d_alphas, int horizon,
+                               int param_dtype, int normalize, float inv_coeff_sum, double* d_sums,
+                               int32_t* d_flags, int max_ctas, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_table(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_keys == nullptr || d_alphas == nullptr || d_sums == nullptr || d_flags == nullptr || horizon <= 0)
+    return MUZO_ERR_ARG;
+  const int64_t nchunks = total_items / MUZO_ITEMS_PER_CTA;
+  const int64_t ctas = (max_ctas > 0 && max_ctas < nchunks) ? max_ctas : nchunks;
+  const dim3 grid(static_cast<unsigned>(ctas));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dispatch_dtype(param_dtype, [&](auto d) {
+    constexpr int D = decltype(d)::value;
+    rebuild_kernel<MUZO_NORMAL, D, true><<<grid, kRebuildThreads, 0, s>>>(
+        d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags, nchunks);
   });
   if (st != MUZO_OK) return st;
   return launch_status();

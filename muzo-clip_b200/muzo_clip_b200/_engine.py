@@ -156,7 +156,9 @@ class StepEngine:
         # are already close to the HBM rate)
         self.keep_noise = bool(getattr(opt, "noise_cache", False)) and self.dist == _lib.NORMAL
         self.noise_buffer: torch.Tensor | None = None
+        self._noise_offsets: list[int] = []
         self._kept_seed: int | None = None
+        self._rebuild_kept = False
         self._build_perturb_groups()
         costs = [ns_flops(b.rows, b.cols, max(opt.ns_steps, 1)) for b in blocks]
         self.owner = partition_blocks(costs, world) if world > 1 else [0] * len(blocks)
@@ -218,6 +220,7 @@ class StepEngine:
             self.keep_noise = False
             return
         self.noise_buffer = torch.empty(max(total, 256), dtype=torch.uint8, device=self.device)
+        self._noise_offsets = offsets
         base = self.noise_buffer.data_ptr()
         for g in self.perturb_groups:
             numels = [b.numel for b in g.blocks]
@@ -319,6 +322,10 @@ class StepEngine:
                 pad_views = [stage]
             rsegs, rtot = _lib.plan_segments([b.numel for b in part], [b.tensor.data_ptr() for b in part],
                                              x0_ptrs, self.dist, self.sms, self.max_thr)
+            if self.keep_noise:
+                # the newest history entry can be read from the kept noise (muzo_rebuild_segments_kept)
+                base = self.noise_buffer.data_ptr()
+                rsegs["kept"] = [base + self._noise_offsets[part[int(bi)].index] for bi in rsegs["block_index"]]
             nsegs, ntot = _lib.plan_linear([b.numel for b in part], x0_ptrs, x0_ptrs)
             ch = Chunk(part, rows, cols, code, stat_slot, _lib.to_device_table(rsegs, self.device), len(rsegs), rtot,
                        _lib.to_device_table(nsegs, self.device), ntot, pad_views=pad_views)
@@ -418,6 +425,8 @@ class StepEngine:
         keys_ptr = dev.data_ptr()
         alphas_ptr = keys_ptr + keys.size * 8
 
+        # the newest entry is the projection whose noise the perturbation passes kept
+        self._rebuild_kept = bool(self.keep_noise and horizon and hist[0].seed == self._kept_seed)
         self.state.zero_()
         base = self.state.data_ptr()
         sums_ptr, flags_ptr, stats_ptr = base, base + self.flags_off, base + self.stats_off
@@ -472,9 +481,15 @@ class StepEngine:
         s_sums = sums_ptr + 8 * _lib.NSUMS * ch.slot0
         s_flags = flags_ptr + 4 * ch.slot0
         self._mark("rebuild", True, stream)
-        _lib.launch("muzo_rebuild_segments", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs, ch.rebuild_items,
-                    keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, self.dist, ch.dtype_code, normalize,
-                    inv_cs, s_sums, s_flags, self.sms if self.overlap else 0, sp)
+        max_ctas = self.sms if self.overlap else 0
+        if self._rebuild_kept:
+            _lib.launch("muzo_rebuild_segments_kept", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs,
+                        ch.rebuild_items, keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, ch.dtype_code,
+                        normalize, inv_cs, s_sums, s_flags, max_ctas, sp)
+        else:
+            _lib.launch("muzo_rebuild_segments", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs, ch.rebuild_items,
+                        keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, self.dist, ch.dtype_code,
+                        normalize, inv_cs, s_sums, s_flags, max_ctas, sp)
         self._mark("rebuild", False, stream)
         self._mark("normalize", True, stream)
         _lib.launch("muzo_ns_normalize", ch.norm_table.data_ptr(), n, ch.norm_items, s_sums, s_flags, sp)

@@ -46,7 +46,7 @@ SEGMENT_DTYPE = np.dtype(
         ("threads", np.uint32),
         ("block_index", np.int32),
         ("elem_start", np.int64),
-        ("reserved", np.int64),
+        ("kept", np.uint64),
     ]
 )
 assert SEGMENT_DTYPE.itemsize == 64
@@ -72,6 +72,10 @@ _SIGNATURES = {
     "muzo_perturb_kept_noise": ([_vp, _i32, _i64, _i32, _f32, _vp], _i32),
     "muzo_rebuild_segments": (
         [_vp, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _vp],
+        _i32,
+    ),
+    "muzo_rebuild_segments_kept": (
+        [_vp, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _vp],
         _i32,
     ),
     "muzo_ns_prepare": ([_vp, _i32, _i64, _i32, _vp, _vp, _vp], _i32),
@@ -112,7 +116,8 @@ class MuzoError(RuntimeError):
 # Kernels each compute entry point enqueues (for launch accounting by benchmarks).
 KERNELS_PER_CALL = {
     "muzo_fill_noise": 1, "muzo_perturb_segments": 1, "muzo_perturb_segments_keep_noise": 1,
-    "muzo_perturb_kept_noise": 1, "muzo_rebuild_segments": 1, "muzo_ns_prepare": 1,
+    "muzo_perturb_kept_noise": 1, "muzo_rebuild_segments": 1, "muzo_rebuild_segments_kept": 1,
+    "muzo_ns_prepare": 1,
     "muzo_ns_normalize": 1, "muzo_ns_gemm": 1, "muzo_update_sumsq": 1, "muzo_apply_update": 1,
     "muzo_qk_scale_rows": 1, "muzo_qk_max": 3, "muzo_logits_head_max": 3, "muzo_max_merge": 1,
     "muzo_ns_normalize_noalloc": 3,

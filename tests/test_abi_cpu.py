@@ -142,6 +142,10 @@ _P = 256
     (lambda L: L.muzo_perturb_kept_noise(_P, 1, 1000, 1, 1.0, None), 1),
     (lambda L: L.muzo_perturb_kept_noise(_P, 1, 1024, 9, 1.0, None), 2),
     (lambda L: L.muzo_perturb_kept_noise(None, 0, 0, 9, 1.0, None), 0),          # empty: no-op
+    (lambda L: L.muzo_rebuild_segments_kept(None, 1, 1024, _P, _P, 8, 1, 1, 1.0, _P, _P, 0, None), 1),
+    (lambda L: L.muzo_rebuild_segments_kept(_P, 1, 1024, _P, _P, 0, 1, 1, 1.0, _P, _P, 0, None), 1),
+    (lambda L: L.muzo_rebuild_segments_kept(_P, 1, 1024, _P, None, 8, 1, 1, 1.0, _P, _P, 0, None), 1),
+    (lambda L: L.muzo_rebuild_segments_kept(_P, 1, 1024, _P, _P, 8, 9, 1, 1.0, _P, _P, 0, None), 2),
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 0, 0, 1, 1, 1.0, _P, _P, 0, None), 1),  # horizon
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 1, 1, 1.0, None, _P, 0, None), 1),
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 9, 1, 1.0, _P, _P, 0, None), 2),

@@ -140,14 +140,15 @@ def test_perturb_with_kept_noise_bit_exact(device, block_rows):
         off += (nbytes + 255) // 256 * 256
 
 
-def test_steps_with_noise_cache_match_steps_without(device):
+@pytest.mark.parametrize("block_rows", [None, 48])
+def test_steps_with_noise_cache_match_steps_without(device, block_rows):
     """Projections and steps through the public API: bit-identical weights, projections and step
-    statistics with and without the kept noise."""
+    statistics with and without the kept noise (the passes and the rebuild's newest entry read it)."""
     from muzo_clip_b200 import MuZOClipOptimizer
 
     model = _MixedMats(device)
     twin = copy.deepcopy(model)
-    kw = dict(seed=9, horizon=3, min_history=1, lr=1e-3)
+    kw = dict(seed=9, horizon=3, min_history=1, lr=1e-3, block_rows=block_rows)
     cached = MuZOClipOptimizer(model, noise_cache=True, **kw)
     plain = MuZOClipOptimizer(twin, **kw)
 
@@ -157,6 +158,7 @@ def test_steps_with_noise_cache_match_steps_without(device):
     for _ in range(4):
         assert cached.estimate_projection(lambda: loss(model)) == plain.estimate_projection(lambda: loss(twin))
         assert cached.step() == plain.step()
+        assert cached._engine._rebuild_kept and not plain._engine._rebuild_kept
         for (n1, p1), (_, p2) in zip(model.named_parameters(), twin.named_parameters()):
             assert torch.equal(p1, p2), n1
 
