@@ -511,7 +511,20 @@ def _run_one_case(args) -> int:
         dist_code = _lib.dist_code(args.dist)
         sms, thr = _lib.device_geometry(device)
         keys = torch.tensor(np.arange(1, args.horizon + 1, dtype=np.int64) * 7919, device=device)
-        if args.case == "perturb":
+        if args.case == "perturb" and args.keep:
+            # a later pass of a kept seed: W <- bf16(W + alpha * Zk), Zk written once by a keeping
+            # pass (normal noise); W read + written and Zk read: 6 B per element
+            zk = torch.empty_like(w)
+            segs, total = _lib.plan_segments([numel], [w.data_ptr()], [zk.data_ptr()], _lib.NORMAL, sms, thr)
+            table = _lib.to_device_table(segs, device)
+            _lib.launch("muzo_perturb_segments_keep_noise", table.data_ptr(), len(segs), total, keys.data_ptr(),
+                        _lib.BF16, 1e-3, sp)
+            lsegs, ltotal = _lib.plan_linear([numel], [w.data_ptr()], [zk.data_ptr()])
+            ltable = _lib.to_device_table(lsegs, device)
+            run = lambda: _lib.launch("muzo_perturb_kept_noise", ltable.data_ptr(), len(lsegs), ltotal,  # noqa: E731
+                                      _lib.BF16, 1e-3, sp)
+            nbytes = 6.0 * numel
+        elif args.case == "perturb":
             segs, total = _lib.plan_segments([numel], [w.data_ptr()], None, dist_code, sms, thr)
             table = _lib.to_device_table(segs, device)
             run = lambda: _lib.launch("muzo_perturb_segments", table.data_ptr(), len(segs), total,  # noqa: E731
@@ -536,7 +549,8 @@ def _run_one_case(args) -> int:
             else None
         ms = _event_ms(run, args.steps, stream, flush)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        out.update(numel=numel, dist=args.dist, horizon=args.horizon if args.case == "rebuild" else None,
+        out.update(numel=numel, dist="kept" if args.keep and args.case == "perturb" else args.dist,
+                   horizon=args.horizon if args.case == "rebuild" else None,
                    ms=round(ms, 4), gbs=round(gbs, 1), hbm_frac=round(gbs / peaks["hbm_gbs"], 4),
                    l2="flushed between passes" if flush is not None else "working set larger than L2")
     elif args.case == "qk":
@@ -581,6 +595,8 @@ def main() -> int:
     ap.add_argument("--impl", default="muzo", choices=["muzo", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--keep", action="store_true",
+                    help="perturb case: time a pass that reads kept noise (muzo_perturb_kept_noise)")
     ap.add_argument("--noise-cache", action="store_true",
                     help="keep each projection's noise between its passes (MuZOClipOptimizer(noise_cache=True))")
     ap.add_argument("--sweep", action="store_true",
