@@ -242,3 +242,28 @@ def test_public_api_matches_reference():
         assert checked >= 25  # the loops above did run over the whole surface
     finally:
         sys.path.remove(REF)
+
+
+@pytest.mark.parametrize("rows, cols, batch", [(4096, 14336, 3), (14336, 4096, 2), (1000, 1003, 4), (7, 9, 1),
+                                               (256, 256, 16)])
+def test_newton_schulz_workspace_layout(rows, cols, batch):
+    """The workspace carved from one flat buffer of ns_workspace_bytes: iterate X [2, batch,
+    rows, ld] and A, B [batch, m, ldm] fit, do not overlap, keep 16-byte aligned rows (ld, ldm
+    multiples of 8) and 256-byte aligned bases; a buffer that cannot hold them is refused."""
+    from muzo_clip_b200.newton_schulz import ns_buffers_in, ns_workspace_bytes
+
+    nbytes = ns_workspace_bytes(rows, cols, batch)
+    raw = torch.empty(nbytes, dtype=torch.uint8)
+    buf = ns_buffers_in(raw, rows, cols, batch)
+    m = min(rows, cols)
+    assert buf.ld % 8 == 0 and buf.ld >= cols and buf.ldm % 8 == 0 and buf.ldm >= m
+    assert tuple(buf.x.shape) == (2, batch, rows, buf.ld)
+    assert tuple(buf.a.shape) == tuple(buf.b.shape) == (batch, m, buf.ldm)
+    base = raw.data_ptr()
+    spans = sorted((t.data_ptr() - base, t.data_ptr() - base + t.numel() * t.element_size())
+                   for t in (buf.x, buf.a, buf.b))
+    assert spans[0][0] == 0 and spans[-1][1] <= nbytes
+    assert all(lo % 256 == 0 for lo, _ in spans)
+    assert all(spans[i][1] <= spans[i + 1][0] for i in range(len(spans) - 1))
+    with pytest.raises(ValueError):  # one byte short of the last view
+        ns_buffers_in(raw[: spans[-1][1] - 1], rows, cols, batch)
