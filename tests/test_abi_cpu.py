@@ -184,3 +184,16 @@ def test_entry_points_reject_bad_arguments_before_any_launch(call, expected):
     from muzo_clip_b200 import _lib
 
     assert call(_lib.lib) == expected
+
+
+def test_segment_layout_matches_header():
+    """muzo_segment's fields (order, names, sizes) in the header equal the binding's dtype."""
+    from muzo_clip_b200 import _lib
+
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "muzo_b200.h").read_text(), flags=re.S)
+    body = re.search(r"typedef struct muzo_segment \{(.*?)\} muzo_segment;", text, flags=re.S).group(1)
+    fields = re.findall(r"(void\*|u?int\d+_t)\s+(\w+);", body)
+    size = {"void*": 8, "int64_t": 8, "uint64_t": 8, "int32_t": 4, "uint32_t": 4}
+    assert [name for _, name in fields] == list(_lib.SEGMENT_DTYPE.names)
+    assert [size[t] for t, _ in fields] == [_lib.SEGMENT_DTYPE[n].itemsize for n in _lib.SEGMENT_DTYPE.names]
+    assert sum(size[t] for t, _ in fields) == _lib.SEGMENT_DTYPE.itemsize == 64
