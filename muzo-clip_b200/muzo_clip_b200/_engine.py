@@ -165,6 +165,10 @@ class StepEngine:
         self.owned = [b for b in blocks if self.owner[b.index] == rank]
         self._step_ready = False
         self._phase_events = None
+        # optional observer of every batch's Newton-Schulz result, called as
+        # hook(blocks, x, stream) with x the [batch, rows, cols] bf16 result in the matrices' own
+        # layout, after the GEMMs and before the update is applied (parity tests read it there)
+        self.ns_output_hook = None
         # rebuild of batch i+1 on a side stream (one CTA per SM) while batch i is on the tensor
         # cores; off by default: the GEMMs already run at the power cap
         self.overlap = os.environ.get("MUZO_OVERLAP_REBUILD", "0") == "1"
@@ -512,6 +516,9 @@ class StepEngine:
         if ch.pad_views is not None:
             with torch.cuda.stream(stream):
                 ch.pad_views[0].copy_(ch.buf.x_slot(parity)[:n, :, : ch.cols])
+        if self.ns_output_hook is not None:
+            x = ch.pad_views[0] if ch.pad_views is not None else ch.buf.x_slot(parity)[:n]
+            self.ns_output_hook(ch.blocks, x, stream)
         table, items = ch.apply_tables[parity if ch.pad_views is None else 0]
         self._mark("apply", True, stream)
         _lib.launch("muzo_update_sumsq", table.data_ptr(), n, items, ch.scales.data_ptr(), s_sums, s_flags, sp)

@@ -126,6 +126,24 @@ def test_newton_schulz_oracle_against_golden(shape):
     assert X.shape == G.shape
 
 
+@pytest.mark.parametrize("shape", ["64x96", "96x64", "256x688", "688x256"])
+def test_exact_ns_torch_matches_oracle(shape):
+    """The torch float64 exact-accumulation iteration (the GPU tests' large-shape checker) is the
+    numpy oracle's exact iteration: both accumulate in float64, so they may differ only where the
+    two BLAS libraries' float64 sums round to different fp32 values (a handful of elements)."""
+    import torch
+    from exact_ns import ns5_exact
+
+    G = STEP[f"ns.{shape}.G"]
+    want = orc.ns5_bf16(G, 5, exact=True)
+    got = ns5_exact(torch.from_numpy(np.ascontiguousarray(G))).numpy()
+    assert got.shape == want.shape
+    rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    assert np.mean(got == want) > 0.99 and rel < 1e-3, (np.mean(got == want), rel)
+    z = np.zeros((8, 8), np.float32)
+    assert not ns5_exact(torch.from_numpy(z)).any()
+
+
 @pytest.mark.parametrize("tag", ["clip", "noclip"])
 def test_apply_matches_golden(tag):
     w0 = STEP[f"apply.{tag}.w0"]
