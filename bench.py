@@ -13,8 +13,9 @@ to +-3, random 63-bit seeds. Synthetic data; 14 GB of weights, far larger than L
 
 N > 1 runs under torchrun: every rank holds a replica, perturbs it locally, and rebuilds /
 orthogonalises / applies the matrices it owns (LPT partition by Newton-Schulz FLOPs); NCCL
-broadcasts the updated weights. ``--impl reference`` times the CPU oracle (the reference's
-algorithm restated) on the host cores on a bounded sample, extrapolated to the full step.
+broadcasts the updated weights. ``--impl reference`` times the reference's op sequence on CPU
+tensors (one matrix per timed step, the four shape classes in turn) on the host cores,
+extrapolated to the full step.
 """
 
 from __future__ import annotations
@@ -170,37 +171,24 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-# ---------------------------------------------------------------- CPU oracle baseline
+# ---------------------------------------------------------------- CPU baseline
 
 
-def _extrapolate_ms(wall: float, phases: list, workers: int) -> float:
-    """Per-step milliseconds of the 8B step from one batch of `workers` blocks run at once: the
-    batch's wall time per block, split by the blocks' own phase times; element-wise phases
-    scale by element count, Newton-Schulz by FLOPs."""
-    from cpu_baseline import COLS, ROWS
+def _cpu_baseline_module():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_baseline
 
-    tot = np.sum(np.asarray(phases, dtype=np.float64), axis=0)
-    frac = tot / max(float(tot.sum()), 1e-12)
-    elem_scale = total_numel() / (ROWS * COLS)
-    m_, n_ = min(ROWS, COLS), max(ROWS, COLS)
-    flop_scale = ns_flops_total() / (5 * (4.0 * m_ * m_ * n_ + 2.0 * m_ ** 3))
-    return 1e3 * (wall / workers) * ((frac[0] + frac[1] + frac[3]) * elem_scale + frac[2] * flop_scale)
-
-
-def _sample_text(workers: int, walls: list[float]) -> str:
-    return (f"oracle, one 1024x4096 bf16 block per host core ({workers} blocks per batch, one thread each: "
-            f"3 perturb passes, H=8 normal rebuild, NS5, apply; batch wall {', '.join(f'{w:.1f}' for w in walls)} s); "
-            f"extrapolated to 224 matrices (element-wise by element count x1664, NS by FLOPs x6891)")
+    return cpu_baseline
 
 
 def cpu_sample_ms(seed: int = 0) -> tuple[float, str, int]:
-    """The oracle (numpy restatement of the reference's arithmetic) through the whole step on
-    all host cores at once (one k_proj-shaped block per core), extrapolated to the 8B step."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    from cpu_baseline import throughput_sample
-
-    wall, phases, workers = throughput_sample(seed)
-    return _extrapolate_ms(wall, phases, workers), _sample_text(workers, [wall]), workers
+    """The reference's op sequence on CPU tensors, one matrix of each of the four shape classes
+    (all host threads), extrapolated to the 224-matrix step."""
+    cb = _cpu_baseline_module()
+    threads = cb.use_all_threads()
+    samples = {c: [sum(cb.matrix_step(c, seed + c))] for c in range(len(cb.CLASSES))}
+    ms = cb.step_ms({c: statistics.median(v) for c, v in samples.items()})
+    return ms, cb.describe(samples, threads), threads
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -393,25 +381,25 @@ def run_gpu(args) -> int:
 
 
 def run_reference(args) -> int:
+    """The reference's CPU implementation of the path on the host cores: every timed step is one
+    matrix of one shape class (the classes in turn, so K steps cover all four when K >= 4), and the
+    reported step time is the 224-matrix step extrapolated by count from each class's median.
+    Warm-up steps run the smallest class."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    sys.path.insert(0, str(ROOT / "oracle"))
-    from cpu_baseline import HostPool
-
-    # each step is one batch of ~10-30 s on all cores: at most one untimed and three timed
-    # batches, whatever --steps / --warmup ask, so the arm ends within a few minutes
-    vals, walls = [], []
-    with HostPool() as pool:
-        threads = pool.workers
-        for i in range(min(args.warmup, 1) + min(args.steps, 3)):
-            wall, phases = pool.batch(seed=i * pool.workers)
-            if i >= min(args.warmup, 1):
-                vals.append(_extrapolate_ms(wall, phases, pool.workers))
-                walls.append(wall)
-    v = statistics.median(vals)
-    sample = _sample_text(threads, walls) + f"; median of {len(vals)} batches"
+    cb = _cpu_baseline_module()
+    threads = cb.use_all_threads()
+    for w in range(args.warmup):
+        cb.matrix_step(0, 1000 + w)
+    ncls = len(cb.CLASSES)
+    samples: dict[int, list[float]] = {c: [] for c in range(ncls)}
+    for i in range(max(args.steps, ncls)):
+        c = i % ncls
+        samples[c].append(sum(cb.matrix_step(c, i)))
+    v = cb.step_ms({c: statistics.median(t) for c, t in samples.items()})
+    sample = cb.describe(samples, threads)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "ms/step", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1), "higher_is_better": False,

@@ -1,102 +1,90 @@
-"""CPU baseline of the optimizer step on the host cores — TEST / BENCHMARK INFRASTRUCTURE ONLY.
+"""CPU baseline of the optimizer step on the host cores — BENCHMARK INFRASTRUCTURE ONLY.
 
-Runs the oracle (``muzo_oracle``, the numpy restatement of the reference's arithmetic) through
-one optimizer step on one Llama-3-8B k_proj-shaped bf16 block (1024 x 4096): three
-perturbation passes, the H-step normal-noise momentum rebuild, five Newton-Schulz iterations and
-the update. ``throughput_sample`` runs one such block per host core in a spawn process pool
-(BLAS limited to one thread per worker, so the cores are not oversubscribed; at most 32
-workers) and reports the
-wall time of the whole batch with each worker's phase split; the caller extrapolates to the full
-model. Only ``bench.py`` uses it, for its reported CPU baseline and its reference arm.
+Runs the reference's own op sequence (``torch_reference``: the torch ops of
+muzo_clip/muzo_optimizer.py:190-357 and newton_schulz.py:17-66, in the same order and dtypes) on
+CPU tensors with all the host threads torch may use, one Llama-3-8B matrix at a time: three
+perturbation passes (+eps, -2eps, +eps), the H = 8 normal-noise momentum rebuild, Newton-Schulz
+(the reference's CPU branch: fp32) and the scale / clip / apply / decay update. The step of the
+whole model is extrapolated from one matrix of each of the four shape classes (per layer: two
+4096 x 4096, two 1024 x 4096, two 14336 x 4096 and one 4096 x 14336), by count. Only
+``bench.py`` uses it, for its reported CPU baseline and its reference arm.
 """
 
 from __future__ import annotations
 
-import multiprocessing as mp
 import os
+import random
 import time
-from concurrent.futures import ProcessPoolExecutor
 
-import numpy as np
+import torch
 
-ROWS, COLS = 1024, 4096
+import torch_reference as tr
+
+# (rows, cols), a parameter name of that shape, matrices of the class per decoder layer
+CLASSES = (
+    ((1024, 4096), "model.layers.0.self_attn.k_proj.weight", 2),
+    ((4096, 4096), "model.layers.0.self_attn.q_proj.weight", 2),
+    ((14336, 4096), "model.layers.0.mlp.gate_proj.weight", 2),
+    ((4096, 14336), "model.layers.0.mlp.down_proj.weight", 1),
+)
+LAYERS = 32
+HORIZON = 8
 
 
-def block_step(seed: int, horizon: int = 8) -> tuple[float, float, float, float]:
-    """Seconds spent in (perturbation passes, rebuild, Newton-Schulz, update) for one block."""
-    import muzo_oracle as orc
+class _Item:
+    def __init__(self, seed: int, p: float):
+        self.seed, self.p = seed, p
 
-    rng = np.random.default_rng(seed)
-    w = orc.bf16_round(rng.standard_normal((ROWS, COLS), dtype=np.float32) * 0.02)
-    keys = [int(k) for k in rng.integers(0, 2**63 - 1, size=horizon + 1, dtype=np.int64)]
-    ps = np.clip(rng.standard_normal(horizon), -3, 3)
+
+def host_threads() -> int:
+    """Host threads this process may run on; torch's intra-op pool is set to that many."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    return max(1, n)
+
+
+def use_all_threads() -> int:
+    torch.set_num_threads(host_threads())
+    return torch.get_num_threads()
+
+
+@torch.no_grad()
+def matrix_step(cls: int, seed: int = 0) -> tuple[float, float, float, float]:
+    """Seconds spent on one bf16 matrix of shape class `cls` in (perturbation passes, rebuild,
+    Newton-Schulz, update)."""
+    (rows, cols), name, _ = CLASSES[cls]
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn((rows, cols), generator=g) * 0.02).to(torch.bfloat16)
+    rng = random.Random(seed)
+    hist = [_Item(rng.randrange(0, 2**63 - 1), max(-3.0, min(3.0, rng.gauss(0, 1)))) for _ in range(HORIZON)]
+    pseed = rng.randrange(0, 2**63 - 1)
+    named = [(name, w)]
     t0 = time.perf_counter()
-    for alpha in (1e-3, -2e-3, 1e-3):
-        w = orc.perturb(w, keys[0], alpha, "normal", "bf16")
+    for s in (1.0, -2.0, 1.0):
+        tr.perturb(named, pseed, s, 1e-3, "normal")
     t1 = time.perf_counter()
-    coeffs = [0.9 ** a for a in range(horizon)]
-    m = orc.rebuild((ROWS, COLS), keys[1:], [c * p for c, p in zip(coeffs, ps)], "normal", "bf16",
-                    float(np.float32(1.0) / np.float32(sum(coeffs))))
+    M = tr.rebuild(w, name, 0, hist, 0.9, "normal", True)
     t2 = time.perf_counter()
-    x = orc.ns5_bf16(m, 5)
+    U = tr.newton_schulz(M, 5)
     t3 = time.perf_counter()
-    orc.apply_update(w, x, 1e-5, 0.2, 0.01, 0.01, "bf16")
+    tr.apply_update(w, U, 1e-5, 0.2, 0.01, 0.01)
     t4 = time.perf_counter()
     return t1 - t0, t2 - t1, t3 - t2, t4 - t3
 
 
-def _worker_init(oracle_dir: str) -> None:
-    import sys
-
-    if oracle_dir not in sys.path:
-        sys.path.insert(0, oracle_dir)
-    try:
-        from threadpoolctl import threadpool_limits
-
-        threadpool_limits(1)
-    except Exception:
-        os.environ["OMP_NUM_THREADS"] = "1"
-    import muzo_oracle  # noqa: F401  (imported before the timed batch)
+def step_ms(seconds_by_class: dict[int, float]) -> float:
+    """Milliseconds of the whole 224-matrix step from one matrix's seconds per class."""
+    return 1e3 * LAYERS * sum(CLASSES[c][2] * s for c, s in seconds_by_class.items())
 
 
-def _ready(_: int) -> int:
-    time.sleep(1.0)  # concurrent sleepers make the executor start every worker
-    return os.getpid()
-
-
-class HostPool:
-    """One spawn worker per host core (started and initialised on entry), reusable for several
-    timed batches."""
-
-    MAX_WORKERS = 32  # every spawn worker re-imports the caller's main module
-
-    def __init__(self, workers: int | None = None):
-        try:
-            usable = len(os.sched_getaffinity(0))
-        except (AttributeError, OSError):
-            usable = os.cpu_count() or 1
-        self.workers = workers or max(1, min(usable, self.MAX_WORKERS))
-        self._ex = None
-
-    def __enter__(self) -> "HostPool":
-        ctx = mp.get_context("spawn")
-        self._ex = ProcessPoolExecutor(max_workers=self.workers, mp_context=ctx, initializer=_worker_init,
-                                       initargs=(os.path.dirname(os.path.abspath(__file__)),))
-        list(self._ex.map(_ready, range(self.workers)))  # every worker started and initialised
-        return self
-
-    def __exit__(self, *exc) -> None:
-        self._ex.shutdown()
-
-    def batch(self, seed: int = 0) -> tuple[float, list[tuple]]:
-        """One block per worker, all at once: the batch's wall seconds and every block's phases."""
-        t0 = time.perf_counter()
-        phases = list(self._ex.map(block_step, range(seed, seed + self.workers)))
-        return time.perf_counter() - t0, phases
-
-
-def throughput_sample(seed: int = 0, workers: int | None = None) -> tuple[float, list[tuple], int]:
-    """One timed batch on a fresh pool: (wall seconds, per-block phase times, worker count)."""
-    with HostPool(workers) as pool:
-        wall, phases = pool.batch(seed)
-        return wall, phases, pool.workers
+def describe(samples: dict[int, list[float]], threads: int) -> str:
+    parts = []
+    for c, times in sorted(samples.items()):
+        (r, k), _, n = CLASSES[c]
+        parts.append(f"{r}x{k}: {len(times)} x {min(times):.1f}-{max(times):.1f} s (x{n * LAYERS})")
+    return (f"the reference's torch op sequence on CPU tensors, {threads} torch threads (nproc "
+            f"{os.cpu_count()}): one bf16 matrix per sample through 3 perturbation passes, the H=8 "
+            f"normal-noise rebuild, fp32 Newton-Schulz (the reference's CPU branch) and the update; "
+            f"{'; '.join(parts)}; the 224-matrix step extrapolated by count from each class's median")

@@ -1,11 +1,13 @@
-"""The reference's PyTorch path for the optimizer hot path, restated op for op — TEST INFRASTRUCTURE.
+"""The reference's PyTorch path for the optimizer hot path, restated op for op — TEST AND BENCHMARK
+INFRASTRUCTURE (the oracle of the torch-level behaviour; the product never imports it).
 
 turfur44/MuZO-Clip computes everything with PyTorch ops; on a B200 those ops *are* the reference
 behaviour (torch's CUDA Philox generator, element-wise kernels, cuBLAS bf16 GEMMs). The reference
-package is not available where the GPU tests run, so this module repeats its tensor-op sequence
-(same ops, same order, same dtypes) for the parity tests and the golden-vector generator.
-``check_against_reference.py`` proves the restatement equal to the real package, bit for bit, on
-CPU tensors in the build container.
+package cannot be assumed importable where the GPU tests run, so this module repeats its
+tensor-op sequence (same ops, same order, same dtypes) for the parity tests, the golden-vector
+generator and the CPU baseline of bench.py. tests/test_reference_link_cpu.py (CPU tensors) and
+tests/test_reference_link_gpu.py (CUDA tensors, the bf16 Newton-Schulz branch) prove it equal to
+the real package, bit for bit, wherever that package can be imported.
 
 Line references are to the reference's muzo_clip/ package.
 """

@@ -1,10 +1,15 @@
-"""Prove tests/golden/torch_reference.py equal to the real reference package, bit for bit.
+"""Prove oracle/torch_reference.py equal to the real reference package, bit for bit — TEST
+INFRASTRUCTURE.
 
-Runs in the build container only (the reference is mounted there, not on GPU machines), on CPU
-tensors: both sides issue the same PyTorch ops, so every result must match exactly. Also writes
-tests/golden/hash_kat.json, the reference's own hash64_seed outputs.
+Both sides issue the same PyTorch ops, so every result must match exactly on the same device:
+``check_all(device)`` runs the comparisons (hash64_seed, make_zo_noise_like, the Newton-Schulz
+iteration, a full step and a perturbation sweep through the reference's own optimizer).
+``tests/test_reference_link_cpu.py`` runs them on CPU tensors (the reference's fp32 branch of
+newton_schulz.py:46) and ``tests/test_reference_link_gpu.py`` on CUDA tensors (its bf16 branch,
+cuBLAS), wherever the reference package can be imported (``reference_pkg``). As a script it also
+writes tests/golden/hash_kat.json, the reference's own hash64_seed outputs.
 
-Usage: python tests/golden/check_against_reference.py [--reference /root/reference]
+Usage: python tests/golden/check_against_reference.py [--reference DIR] [--device cpu|cuda]
 """
 
 from __future__ import annotations
@@ -20,18 +25,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
+sys.path.insert(0, str(HERE.parents[1] / "oracle"))
 
 import torch_reference as tr  # noqa: E402
-
-
-def _tiny_model(dtype=torch.float32):
-    from transformers import LlamaConfig, LlamaForCausalLM
-
-    torch.manual_seed(0)
-    cfg = LlamaConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
-                      intermediate_size=96, vocab_size=128, attn_implementation="eager")
-    return LlamaForCausalLM(cfg).to(dtype)
-
 
 HASH_CASES = [
     (12345, "model.layers.0.self_attn.q_proj.weight", (4096, 4096), 0),
@@ -43,44 +39,56 @@ HASH_CASES = [
 ]
 
 
-def main() -> int:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
-    args = ap.parse_args()
-    sys.path.insert(0, args.reference)
-    from muzo_clip import MuZOClipOptimizer, zeropower_via_newtonschulz5
-    from muzo_clip.muzo_optimizer import HistoryItem
-    from muzo_clip.prng import hash64_seed, make_zo_noise_like
+def _tiny_model(device, dtype=torch.float32):
+    from transformers import LlamaConfig, LlamaForCausalLM
 
-    # 1. hash known answers
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      intermediate_size=96, vocab_size=128, attn_implementation="eager")
+    return LlamaForCausalLM(cfg).to(dtype).to(device)
+
+
+def hash_kat(ref) -> list[dict]:
+    """The reference's hash64_seed on HASH_CASES, checked against the restatement."""
     kat = []
     for seed, name, shape, bi in HASH_CASES:
-        ref = hash64_seed(seed, name, shape, bi)
-        assert tr.hash64_seed(seed, name, shape, bi) == ref
-        kat.append({"seed": seed, "name": name, "shape": list(shape), "block": bi, "key": ref})
-    (HERE / "hash_kat.json").write_text(json.dumps(kat, indent=1) + "\n")
+        key = ref.prng.hash64_seed(seed, name, shape, bi)
+        assert tr.hash64_seed(seed, name, shape, bi) == key
+        kat.append({"seed": seed, "name": name, "shape": list(shape), "block": bi, "key": key})
+    return kat
 
-    # 2. noise (CPU generator): same ops, same values
+
+def check_noise(ref, device) -> None:
     for dist in ("normal", "rademacher"):
-        for dtype in (torch.float32, torch.bfloat16):
-            t = torch.zeros((33, 17), dtype=dtype)
-            a = make_zo_noise_like(t, 7, "x.weight", 2, dist)
-            b = tr.noise_like(t, 7, "x.weight", 2, dist)
-            assert torch.equal(a, b), (dist, dtype)
+        for dtype in (torch.float32, torch.bfloat16, torch.float16):
+            for shape in ((33, 17), (1000, 1031)):
+                t = torch.zeros(shape, dtype=dtype, device=device)
+                a = ref.prng.make_zo_noise_like(t, 7, "x.weight", 2, dist)
+                b = tr.noise_like(t, 7, "x.weight", 2, dist)
+                assert torch.equal(a, b), (dist, dtype, shape)
 
-    # 3. Newton-Schulz (CPU path)
-    g = torch.Generator().manual_seed(3)
-    for shape in ((24, 40), (40, 24)):
-        G = torch.randn(shape, generator=g)
-        assert torch.equal(zeropower_via_newtonschulz5(G, 5), tr.newton_schulz(G, 5)), shape
 
-    # 4. a full step against the reference optimizer on a tiny Llama (both distributions,
-    #    with and without row blocks)
+def check_newton_schulz(ref, device) -> None:
+    g = torch.Generator(device="cpu").manual_seed(3)
+    for shape in ((24, 40), (40, 24), (256, 688), (688, 256)):
+        G = torch.randn(shape, generator=g).to(device)
+        for steps in (0, 1, 5):
+            a = ref.newton_schulz.zeropower_via_newtonschulz5(G, steps)
+            assert torch.equal(a, tr.newton_schulz(G, steps)), (shape, steps)
+    z = torch.zeros((16, 16), device=device)
+    assert torch.equal(ref.newton_schulz.zeropower_via_newtonschulz5(z), tr.newton_schulz(z))
+
+
+def check_step_and_perturb(ref, device, dtype=torch.float32) -> None:
+    """A full step() of the reference optimizer on a tiny Llama against torch_reference.step on a
+    twin (both distributions, with and without row blocks), then a perturbation sweep."""
+    from muzo_clip.muzo_optimizer import HistoryItem
+
     for dist, block_rows in (("normal", None), ("rademacher", None), ("normal", 40)):
-        model = _tiny_model()
+        model = _tiny_model(device, dtype)
         twin = copy.deepcopy(model)
-        opt = MuZOClipOptimizer(model, seed=11, distribution=dist, block_rows=block_rows, lr=1e-2,
-                                update_ratio_clip=0.05)
+        opt = ref.MuZOClipOptimizer(model, seed=11, distribution=dist, block_rows=block_rows, lr=1e-2,
+                                    update_ratio_clip=0.05)
         rng = random.Random(5)
         for _ in range(6):
             opt.history.append(HistoryItem(seed=rng.randrange(0, 2**63 - 1), p=rng.uniform(-3, 3), p_raw=0.0,
@@ -95,13 +103,34 @@ def main() -> int:
             assert mine[key] == stats[key], (dist, key, mine[key], stats[key])
         for (n1, p1), (n2, p2) in zip(model.named_parameters(), twin.named_parameters()):
             assert torch.equal(p1, p2), (dist, n1)
-
-        # perturbation sweep
         tr.perturb(named, 99, 1.0, opt.zo_eps, dist, block_rows)
         opt._perturb_selected(99, 1.0)
         for (n1, p1), (n2, p2) in zip(model.named_parameters(), twin.named_parameters()):
             assert torch.equal(p1, p2), (dist, "perturb", n1)
-    print("torch_reference matches the reference package on CPU:", len(kat), "hash cases, noise, NS, step, perturb")
+
+
+def main() -> int:
+    from reference_pkg import reference_path
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=None, help="directory holding the muzo_clip package")
+    ap.add_argument("--device", default="cpu")
+    args = ap.parse_args()
+    root = args.reference or reference_path()
+    if root is None:
+        raise SystemExit("reference package not found: pass --reference or set MUZO_REFERENCE_PATH")
+    sys.path.insert(0, str(root))
+    import muzo_clip as ref
+    import muzo_clip.newton_schulz  # noqa: F401
+    import muzo_clip.prng  # noqa: F401
+
+    device = torch.device(args.device)
+    kat = hash_kat(ref)
+    (HERE / "hash_kat.json").write_text(json.dumps(kat, indent=1) + "\n")
+    check_noise(ref, device)
+    check_newton_schulz(ref, device)
+    check_step_and_perturb(ref, device)
+    print("torch_reference matches the reference package on", device, ":", len(kat), "hash cases, noise, NS, step, perturb")
     return 0
 
 

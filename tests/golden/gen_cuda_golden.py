@@ -1,6 +1,6 @@
 """Generate the CUDA golden vectors of the reference path with torch on a B200.
 
-Runs the reference's tensor-op sequence (torch_reference.py, itself proven equal to the reference
+Runs the reference's tensor-op sequence (oracle/torch_reference.py, itself proven equal to the reference
 package by check_against_reference.py) on a CUDA device and stores small fixtures:
   noise_cuda.npz    torch CUDA generator output for several sizes (full arrays for small tensors,
                     fixed index samples for large ones, including tensors torch splits into
@@ -22,6 +22,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
+sys.path.insert(0, str(HERE.parents[1] / "oracle"))
 
 import torch_reference as tr  # noqa: E402
 

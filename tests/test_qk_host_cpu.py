@@ -102,11 +102,12 @@ def test_qk_scaling_host_logic_matches_reference(monkeypatch, dtype, hq, hkv, q_
     the head count exercises the whole-matrix fallback."""
     import copy
     import sys
-    from pathlib import Path
 
-    ref_root = Path("/root/reference")
-    if not (ref_root / "muzo_clip" / "qk_clip.py").exists():
-        pytest.skip("reference package not mounted")
+    from reference_pkg import reference_path
+
+    ref_root = reference_path()
+    if ref_root is None:
+        pytest.skip("reference package not available (MUZO_REFERENCE_PATH / baseline/_ref)")
     sys.path.insert(0, str(ref_root))
     from muzo_clip.qk_clip import QKClipController as RefController
 
