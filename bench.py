@@ -152,6 +152,7 @@ class ClockSampler:
 # ns_gemm launches of one step (794.4 GB over the 2 captured steps), and per perturbation pass.
 NS_DRAM_BYTES_PER_STEP = 397.2e9
 PERTURB_DRAM_BYTES_PER_PASS = 27.89e9
+TRAFFIC_SOURCE = "profiles/launches_dram_llama3_8b_step.md (one ncu capture, not measured in this run)"
 
 
 def ns_operand_bytes(rows: int, cols: int, steps: int = 5) -> float:
@@ -299,8 +300,10 @@ def run_gpu(args) -> int:
         rebuild_ms = max(phases.get("rebuild", 0.0), 1e-9)
         rebuild_samples = float(HORIZON) * owned_elems
         rebuild_bytes = 4.0 * owned_elems
-        update_ms = max(phases.get("normalize", 0.0) + phases.get("apply", 0.0), 1e-9)
-        update_bytes = 12.0 * owned_elems
+        apply_ms = max(phases.get("apply", 0.0), 1e-9)
+        apply_bytes = 6.0 * owned_elems        # update read (bf16), W read, W written
+        norm_ms = max(phases.get("normalize", 0.0), 1e-9)
+        norm_bytes = 4.0 * owned_elems         # bf16 momentum read and written
         h2d = 8 * len(engine.blocks) * 3 + 8 * len(engine.owned) * HORIZON + 4 * HORIZON
         d2h = engine.state_bytes + 16
         line = {
@@ -339,15 +342,16 @@ def run_gpu(args) -> int:
                 "executed_frac": round(ns_exec_tflops / peaks["bf16_tflops_sustained"], 4),
                 "peak_source": f"{peaks['source']} bf16 sustained",
                 "traffic": NS_DRAM_BYTES_PER_STEP if world == 1 else None,
-                "traffic_unit": "DRAM bytes per step, all ns_gemm launches (ncu capture of this workload, 1 GPU)",
+                "traffic_unit": "DRAM bytes per step, all ns_gemm launches",
+                "traffic_source": TRAFFIC_SOURCE,
                 "operand_bytes": round(ns_bytes_min),
             },
             "perturb_roofline": {
                 "bound": "hbm", "achieved": round(perturb_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(perturb_gbs / peaks["hbm_gbs"], 4), "peak_source": f"{peaks['source']} copy",
                 "rademacher_achieved": round(rad_gbs, 1), "rademacher_frac": round(rad_gbs / peaks["hbm_gbs"], 4),
-                "traffic": PERTURB_DRAM_BYTES_PER_PASS, "traffic_unit": "DRAM bytes per pass (ncu)",
-                "algorithmic_bytes": perturb_bytes,
+                "traffic": PERTURB_DRAM_BYTES_PER_PASS, "traffic_unit": "DRAM bytes per pass",
+                "traffic_source": TRAFFIC_SOURCE, "algorithmic_bytes": perturb_bytes,
             },
             # the rebuild regenerates H normal samples per weight: its bound is the instruction
             # issue rate (ncu: 43 instructions per sample, 74 % issue utilisation), not HBM
@@ -357,12 +361,20 @@ def run_gpu(args) -> int:
                 "hbm_frac": round(rebuild_bytes / (rebuild_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                 "algorithmic_bytes": rebuild_bytes,
             },
-            # normalisation (bf16 read + write), the update's sum of squares (bf16 read) and the
-            # apply (update and W read, W written): 12 B per owned weight
+            # the apply (update and W read, W written: 6 B per owned weight; the update's sum of
+            # squares comes from the last Newton-Schulz GEMM's epilogue) and, separately, the
+            # normalisation of the rebuilt momentum (4 B per owned weight)
             "update_roofline": {
-                "bound": "hbm", "achieved": round(update_bytes / (update_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "peak": peaks["hbm_gbs"], "frac": round(update_bytes / (update_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
-                "algorithmic_bytes": update_bytes,
+                "bound": "hbm", "kernel": "apply_update_kernel",
+                "achieved": round(apply_bytes / (apply_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "peak": peaks["hbm_gbs"], "frac": round(apply_bytes / (apply_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                "algorithmic_bytes": apply_bytes,
+            },
+            "normalize_roofline": {
+                "bound": "hbm", "kernel": "ns_normalize_kernel",
+                "achieved": round(norm_bytes / (norm_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "peak": peaks["hbm_gbs"], "frac": round(norm_bytes / (norm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                "algorithmic_bytes": norm_bytes,
             },
             "e2e": {"value": round(wall_ms, 3), "unit": "ms/step", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},

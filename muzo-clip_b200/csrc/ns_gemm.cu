@@ -35,7 +35,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int MN_CHUNK_BYTES = 64 * BK * 2;  // one 64(MN) x 64(K) box of an MN-major operand
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 2 * BN;       // two accumulators of BN fp32 columns
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers, flags*/;
 
 using namespace tc;
 
@@ -72,11 +72,50 @@ struct GemmArgs {
   float c1, c2;
   int32_t* status;
   int32_t* sched;          // CTA-pair kernel: [0] next tile, [1] pairs finished (zero between launches)
+  // update epilogue of the last iteration: per batch index b, sums[b * MUZO_NSUMS + MUZO_SUM_U2]
+  // += sum of (fp32(D) * scales[b])^2 and flags[b] |= MUZO_FLAG_NONFINITE_OUTPUT (null: off)
+  double* sums;
+  const float* scales;
+  int32_t* flags;
+};
+
+// Stall request read from status word 3 at kernel start (test use): the named role waits on a
+// barrier nothing arrives at, for kStallLimitCycles, and then takes the timeout path.
+constexpr unsigned long long kStallLimitCycles = kWaitLimitCycles / 8;
+
+// Sum of squares of the stored (bf16-rounded) values times `scale`, in the order of the separate
+// update_sumsq pass: an fp32 chain over each 8 values, added in fp64.
+struct U2Acc {
+  double sum = 0.0;
+  bool finite = true;
+  __device__ __forceinline__ void add8(const float* v, float scale, int count) {
+    float p = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < count) {
+        finite = finite && isfinite(v[k]);
+        const float u = v[k] * scale;
+        p = __fmaf_rn(u, u, p);
+      }
+    }
+    sum += p;
+  }
+  // One atomic per warp and tile; `b` is the tile's batch index.
+  __device__ __forceinline__ void flush(const GemmArgs& g, int64_t b, int lane) {
+    const double t = warp_sum(sum);
+    const bool all_finite = __all_sync(0xffffffffu, finite) != 0;
+    if (lane == 0) {
+      if (t != 0.0) atomicAdd(g.sums + b * MUZO_NSUMS + MUZO_SUM_U2, t);
+      if (!all_finite) atomicOr(g.flags + b, MUZO_FLAG_NONFINITE_OUTPUT);
+    }
+    sum = 0.0;
+    finite = true;
+  }
 };
 
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, int64_t b, int64_t row, int64_t col0,
-                                               const uint32_t (&acc)[32]) {
+                                               const uint32_t (&acc)[32], U2Acc& u2, float u2_scale) {
   if (row >= g.m || col0 >= g.n) return;
   if (g.sym && col0 + 31 < row) return;  // strictly below the diagonal: written by the mirror
   const int64_t base = b * g.d_bs + row * g.ldd + col0;
@@ -144,9 +183,24 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& g, int64_t b, int
       u.z = pack_bf16(o[8 * q + 4], o[8 * q + 5]);
       u.w = pack_bf16(o[8 * q + 6], o[8 * q + 7]);
       dp[q] = u;
+      if (EPI == MUZO_EPI_UPDATE && g.sums != nullptr) {
+        const float r[8] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y),
+                            bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w)};
+        u2.add8(r, u2_scale, 8);
+      }
     }
   } else {
     for (int i = 0; i < 32 && col0 + i < g.n; ++i) g.d[base + i] = __float2bfloat16_rn(o[i]);
+    if (EPI == MUZO_EPI_UPDATE && g.sums != nullptr) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float r[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) r[k] = bf16r(o[8 * q + k]);
+        const int64_t left = g.n - (col0 + 8 * q);
+        if (left > 0) u2.add8(r, u2_scale, left >= 8 ? 8 : static_cast<int>(left));
+      }
+    }
   }
 }
 
@@ -187,15 +241,18 @@ ns_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* stall_bar = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(stall_bar + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int stall = *reinterpret_cast<volatile int*>(g.status + 3);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
     for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 4); }
+    mbar_init(stall_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -218,7 +275,7 @@ ns_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
       int stage = 0;
       uint32_t phase = 0;
-      bool ok = true;
+      bool ok = stall != kErrTimeoutProducer || mbar_wait(stall_bar, 0, kStallLimitCycles);
       uint32_t armed = 0;            // bit s: stage s received at least one load
       uint32_t armed_parity = 0;     // bit s: phase parity of the last load into stage s
       for (int64_t t = blockIdx.x; t < g.num_tiles && ok; t += gridDim.x) {
@@ -264,7 +321,7 @@ ns_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       constexpr uint32_t idesc = make_idesc(BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
-      bool ok = true;
+      bool ok = stall != kErrTimeoutMma || mbar_wait(stall_bar, 0, kStallLimitCycles);
       int64_t local = 0;
       for (int64_t t = blockIdx.x; t < g.num_tiles && ok; t += gridDim.x, ++local) {
         const int acc = static_cast<int>(local & 1);
@@ -300,7 +357,13 @@ ns_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int lane_base = 32 * (warp & 3);  // TMEM lanes this warp may access
     int64_t local = 0;
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < g.num_tiles; t += gridDim.x, ++local) {
+    if (stall == kErrTimeoutEpilogue) {
+      bool waited = true;
+      if (lane == 0) waited = mbar_wait(stall_bar, 0, kStallLimitCycles);
+      ok = __shfl_sync(0xffffffffu, waited ? 1 : 0, 0) != 0;
+    }
+    U2Acc u2;
+    for (int64_t t = blockIdx.x; t < g.num_tiles && ok; t += gridDim.x, ++local) {
       int64_t b; int tm, tn;
       tile_coords(g, t, b, tm, tn);
       const int acc = static_cast<int>(local & 1);
@@ -311,12 +374,14 @@ ns_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       if (!ready || *reinterpret_cast<volatile int*>(abort_flag)) { ok = ready; break; }
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tm) * BM + lane_base + lane;
+      const float u2_scale = (EPI == MUZO_EPI_UPDATE && g.sums != nullptr) ? g.scales[b] : 0.0f;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(lane_base) << 16) + acc * BN + c * 32, r);
-        epilogue_chunk<EPI>(g, b, row, static_cast<int64_t>(tn) * BN + c * 32, r);
+        epilogue_chunk<EPI>(g, b, row, static_cast<int64_t>(tn) * BN + c * 32, r, u2, u2_scale);
       }
+      if (EPI == MUZO_EPI_UPDATE && g.sums != nullptr) u2.flush(g, b, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty + acc);
@@ -359,7 +424,7 @@ constexpr int P_STAGES = 6;
 constexpr int PA_BYTES = PHALF * BK * 2;   // 16 KB
 constexpr int PB_BYTES = PHALF * BK * 2;   // 16 KB
 constexpr int P_STAGE_BYTES = PA_BYTES + PB_BYTES;
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 512;
 constexpr int TILE_SLOTS = 4;   // tile-index ring from the leader's producer to every other role
 constexpr int TILE_READERS = 10;  // leader MMA + 4 epilogue warps per CTA + the peer's producer
 
@@ -402,21 +467,27 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   uint64_t* drain = tempty + 2;
   uint64_t* tile_full = drain + 1;
   uint64_t* tile_empty = tile_full + TILE_SLOTS;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tile_empty + TILE_SLOTS);
+  uint64_t* stall_bar = tile_empty + TILE_SLOTS;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(stall_bar + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
   int* tile_slots = abort_flag + 1;
+  // phases of each stage this CTA's producer loaded into (leader: armed), read by the leader
+  // after both producers have stopped
+  uint32_t* issued = reinterpret_cast<uint32_t*>(tile_slots + TILE_SLOTS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const int64_t npairs = gridDim.x >> 1;
+  const int stall = *reinterpret_cast<volatile int*>(g.status + 3);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); }
+    for (int s = 0; s < P_STAGES; ++s) { mbar_init(full + s, 1); mbar_init(empty + s, 1); issued[s] = 0; }
     for (int a = 0; a < 2; ++a) { mbar_init(tfull + a, 1); mbar_init(tempty + a, 8); }
     for (int s = 0; s < TILE_SLOTS; ++s) { mbar_init(tile_full + s, 1); mbar_init(tile_empty + s, TILE_READERS); }
     mbar_init(drain, 1);
+    mbar_init(stall_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -438,8 +509,8 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
       int stage = 0;
       uint32_t phase = 0;
-      bool ok = true;
-      uint32_t armed = 0, armed_parity = 0;  // leader: stages armed, and their last parity
+      bool ok = !(leader && stall == kErrTimeoutProducer) || mbar_wait(stall_bar, 0, kStallLimitCycles);
+      uint32_t count[P_STAGES] = {};         // phases loaded into (leader: armed) per stage
       for (int64_t k = 0; ok; ++k) {
         int t = -1;
         if (leader) {
@@ -466,11 +537,9 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           uint8_t* sb = sa + PA_BYTES;
           const uint32_t bar = map_to_rank(smem_u32(full + stage), 0);
-          if (leader) {
-            mbar_arrive_expect_tx_u32(smem_u32(full + stage), 2 * P_STAGE_BYTES);
-            armed |= 1u << stage;
-            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-          }
+          if (leader) mbar_arrive_expect_tx_u32(smem_u32(full + stage), 2 * P_STAGE_BYTES);
+#pragma unroll
+          for (int s2 = 0; s2 < P_STAGES; ++s2) count[s2] += s2 == stage ? 1u : 0u;
           const int k0 = kb * BK;
           if (A_MN) {
 #pragma unroll
@@ -488,10 +557,9 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         }
       }
       if (!ok) { atomicCAS(g.status, kErrNone, kErrTimeoutProducer); pair_abort(abort_flag); }
-      // Every load of both CTAs counts on the leader's barriers: all must have landed before
-      // either CTA may exit (bounded).
-      for (int s2 = 0; s2 < P_STAGES; ++s2)
-        if (armed & (1u << s2)) mbar_wait(full + s2, (armed_parity >> s2) & 1u);
+      // the loads still in flight are waited for after both producers have stopped (below)
+#pragma unroll
+      for (int s2 = 0; s2 < P_STAGES; ++s2) issued[s2] = count[s2];
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -500,7 +568,7 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       constexpr uint32_t idesc = make_idesc(PM, PN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
-      bool ok = true;
+      bool ok = stall != kErrTimeoutMma || mbar_wait(stall_bar, 0, kStallLimitCycles);
       for (int64_t local = 0; ok; ++local) {
         int t = -1;
         if (!read_tile(tile_slots, tile_full, local, t)) { ok = false; break; }
@@ -535,7 +603,13 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     const int lane_base = 32 * (warp & 3);
     const uint32_t leader_tempty0 = map_to_rank(smem_u32(tempty), 0);
     bool ok = true;
-    for (int64_t local = 0;; ++local) {
+    if (stall == kErrTimeoutEpilogue) {
+      bool waited = true;
+      if (lane == 0) waited = mbar_wait(stall_bar, 0, kStallLimitCycles);
+      ok = __shfl_sync(0xffffffffu, waited ? 1 : 0, 0) != 0;
+    }
+    U2Acc u2;
+    for (int64_t local = 0; ok; ++local) {
       int t = -1;
       bool got = true;
       if (lane == 0) {
@@ -556,12 +630,14 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       if (!ready || *reinterpret_cast<volatile int*>(abort_flag)) { ok = ready; break; }
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tm) * PM + static_cast<int64_t>(rank) * PHALF + lane_base + lane;
+      const float u2_scale = (EPI == MUZO_EPI_UPDATE && g.sums != nullptr) ? g.scales[b] : 0.0f;
 #pragma unroll 1
       for (int c = 0; c < PN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(lane_base) << 16) + acc * BN + c * 32, r);
-        epilogue_chunk<EPI>(g, b, row, static_cast<int64_t>(tn) * PN + c * 32, r);
+        epilogue_chunk<EPI>(g, b, row, static_cast<int64_t>(tn) * PN + c * 32, r, u2, u2_scale);
       }
+      if (EPI == MUZO_EPI_UPDATE && g.sums != nullptr) u2.flush(g, b, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
@@ -571,7 +647,25 @@ ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();  // both CTAs past their loops: the abort flag is final in both
+  cluster_sync_all();  // both CTAs past their loops: the abort flag and the load records are final
+  if (warp == 0 && leader && lane == 0) {
+    // Every load of both CTAs counts on the leader's stage barriers, and both CTAs must outlive
+    // them. A producer loads a stage's phase only once the previous phase was consumed, which
+    // needs both CTAs' loads, so the two records differ by at most one phase per stage: after an
+    // abort, the leader supplies the missing arrival (a phase the peer loaded but the leader did
+    // not arm) or the missing bytes (a phase the leader armed but the peer did not load) so that
+    // every phase with a load in flight completes, then waits for it (bounded).
+    const uint32_t peer = map_to_rank(smem_u32(issued), 1);
+    for (int s2 = 0; s2 < P_STAGES; ++s2) {
+      uint32_t np;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(np) : "r"(peer + 4u * s2) : "memory");
+      const uint32_t nl = issued[s2];
+      if (np == nl + 1) mbar_arrive_expect_tx_u32(smem_u32(full + s2), P_STAGE_BYTES);
+      else if (nl == np + 1) mbar_complete_tx(full + s2, P_STAGE_BYTES);
+      const uint32_t n = np > nl ? np : nl;
+      if (n > 0) mbar_wait(full + s2, (n - 1) & 1u);
+    }
+  }
   if (warp == 1 && leader && lane == 0 && *reinterpret_cast<volatile int*>(abort_flag)) {
     // an aborted pair drains its in-flight MMAs before the accumulators are released (bounded)
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(drain))
@@ -693,8 +787,11 @@ extern "C" {
 int muzo_ns_gemm(const void* a, int64_t lda, int64_t a_batch_stride, int a_mn, const void* b, int64_t ldb,
                  int64_t b_batch_stride, int b_mn, void* d, int64_t ldd, int64_t d_batch_stride,
                  const void* e, int epilogue, float c1, float c2, int64_t m, int64_t n, int64_t k,
-                 int64_t batch, int symmetric, int32_t* d_status, void* stream) {
+                 int64_t batch, int symmetric, double* d_sums, const float* d_scales, int32_t* d_flags,
+                 int32_t* d_status, void* stream) {
   if (a == nullptr || b == nullptr || d == nullptr || m <= 0 || n <= 0 || k <= 0 || batch <= 0)
+    return MUZO_ERR_ARG;
+  if (d_sums != nullptr && (epilogue != MUZO_EPI_UPDATE || d_scales == nullptr || d_flags == nullptr))
     return MUZO_ERR_ARG;
   if (epilogue != MUZO_EPI_STORE && e == nullptr) return MUZO_ERR_ARG;
   if (epilogue < MUZO_EPI_STORE || epilogue > MUZO_EPI_UPDATE) return MUZO_ERR_ARG;
@@ -744,6 +841,9 @@ int muzo_ns_gemm(const void* a, int64_t lda, int64_t a_batch_stride, int a_mn, c
   g.d_bs = d_batch_stride ? d_batch_stride : ldd * m;
   g.e = static_cast<const __nv_bfloat16*>(e);
   g.c1 = c1; g.c2 = c2;
+  g.sums = d_sums;
+  g.scales = d_scales;
+  g.flags = d_flags;
   if (d_status == nullptr) {
     void* p = nullptr;
     MUZO_CUDA_CHECK(cudaGetSymbolAddress(&p, g_default_status));

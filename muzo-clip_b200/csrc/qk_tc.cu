@@ -344,6 +344,9 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
   uint64_t* drain = q_empty + PQ_SLOTS;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
+  // phases this CTA's producer loaded into (leader: armed): key stages, then query buffers; read
+  // by the leader once both producers have stopped
+  uint32_t* issued = reinterpret_cast<uint32_t*>(abort_flag + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -357,6 +360,7 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
     for (int q = 0; q < PQ_SLOTS; ++q) { mbar_init(q_full + q, 1); mbar_init(q_empty + q, 1); }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    for (int s = 0; s < PK_MAX_STAGES + PQ_SLOTS; ++s) issued[s] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -378,7 +382,6 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      uint32_t armed = 0, armed_parity = 0;   // leader: K stages armed and their last parity
       int64_t useq = -1;                      // sequence number of the current query block
       PairTileCursor cur;
       cur.start(g, t_begin);
@@ -401,26 +404,21 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
           for (int kb = 0; kb < g.num_kb; ++kb)
             tma_load_4d_pair(&map_q, qbar, sq_slots + qs * PQ_SLOT_BYTES + kb * PQ_SUB_BYTES, kb * QBK,
                              qb * 2 * PQ_ROWS + static_cast<int>(rank) * PQ_ROWS, h, b);
+          issued[PK_MAX_STAGES + qs] += 1;
         }
         const int kvh = h / g.group;
         for (int kb = 0; kb < g.num_kb; ++kb) {
           if (!mbar_wait(empty + stage, phase ^ 1)) { ok = false; break; }
           if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
-          if (leader) {
-            mbar_arrive_expect_tx_u32(smem_u32(full + stage), 2u * PK_STAGE_BYTES);
-            armed |= 1u << stage;
-            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-          }
+          if (leader) mbar_arrive_expect_tx_u32(smem_u32(full + stage), 2u * PK_STAGE_BYTES);
           tma_load_4d_pair(&map_k, map_to_rank(smem_u32(full + stage), 0), sk_stages + stage * PK_STAGE_BYTES,
                            kb * QBK, kv * 2 * PK_ROWS + static_cast<int>(rank) * PK_ROWS, kvh, b);
+          issued[stage] += 1;
           if (++stage == PK_STAGES) { stage = 0; phase ^= 1; }
         }
       }
       if (!ok) { atomicCAS(g.status, kErrNone, kErrTimeoutProducer); pair_abort(abort_flag); atomicExch(g.valid, 0); }
-      for (int s2 = 0; s2 < PK_STAGES; ++s2)
-        if (armed & (1u << s2)) mbar_wait(full + s2, (armed_parity >> s2) & 1u);
-      for (int64_t u = useq - (PQ_SLOTS - 1); leader && u <= useq; ++u)   // last load into each buffer
-        if (u >= 0) mbar_wait(q_full + u % PQ_SLOTS, static_cast<uint32_t>((u / PQ_SLOTS) & 1));
+      // the loads still in flight are waited for after both producers have stopped (below)
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -547,7 +545,28 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
 
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();
+  cluster_sync_all();  // both producers stopped: the load records are final
+  if (warp == 0 && leader && lane == 0) {
+    // Both CTAs' loads count on the leader's barriers. A producer loads a stage's (or query
+    // buffer's) next phase only once the previous one was consumed, which needs both CTAs' loads,
+    // so the two records differ by at most one phase: after an abort the leader supplies the
+    // missing arrival (peer loaded, leader did not arm) or the missing bytes (leader armed, peer
+    // did not load), then waits (bounded) until every phase with a load in flight has landed.
+    const uint32_t peer = map_to_rank(smem_u32(issued), 1);
+    for (int s2 = 0; s2 < PK_STAGES + PQ_SLOTS; ++s2) {
+      const bool qslot = s2 >= PK_STAGES;
+      const int idx = qslot ? PK_MAX_STAGES + (s2 - PK_STAGES) : s2;
+      uint64_t* bar = qslot ? q_full + (s2 - PK_STAGES) : full + s2;
+      const uint32_t bytes = qslot ? static_cast<uint32_t>(g.num_kb * PQ_SUB_BYTES) : PK_STAGE_BYTES;
+      uint32_t np;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(np) : "r"(peer + 4u * idx) : "memory");
+      const uint32_t nl = issued[idx];
+      if (np == nl + 1) mbar_arrive_expect_tx_u32(smem_u32(bar), bytes);
+      else if (nl == np + 1) mbar_complete_tx(bar, bytes);
+      const uint32_t n = np > nl ? np : nl;
+      if (n > 0) mbar_wait(bar, (n - 1) & 1u);
+    }
+  }
   if (warp == 1 && leader && lane == 0 && *reinterpret_cast<volatile int*>(abort_flag)) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(drain))
                  : "memory");

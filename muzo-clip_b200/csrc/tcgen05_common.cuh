@@ -68,15 +68,23 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
-// Bounded wait for the phase with parity `parity` to complete. Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait for the phase with parity `parity` to complete. Returns false once `limit` cycles
+// have passed without it.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit = kWaitLimitCycles) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const long long start = clock64();
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
-    if (static_cast<unsigned long long>(clock64() - start) > kWaitLimitCycles) return false;
+    if (static_cast<unsigned long long>(clock64() - start) > limit) return false;
   }
+}
+
+// Count `bytes` of the current phase's expected transaction as done (bytes that will never arrive).
+__device__ __forceinline__ void mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0,

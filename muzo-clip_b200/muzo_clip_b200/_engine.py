@@ -3,8 +3,8 @@
 Everything model-sized stays on the GPU. Per perturbation pass the host computes one 63-bit key
 per parameter block (cached per seed), uploads them, and one kernel launch per parameter dtype
 regenerates the noise and updates every block in place. Per step the owned blocks are processed
-in batches of equal shape: rebuild -> normalise -> Newton-Schulz GEMMs -> sum of squares ->
-apply, and the step statistics come back in one device-to-host copy.
+in batches of equal shape: rebuild -> normalise -> Newton-Schulz GEMMs (the last one also sums
+the update's squares) -> apply, and the step statistics come back in one device-to-host copy.
 """
 
 from __future__ import annotations
@@ -169,6 +169,9 @@ class StepEngine:
         # hook(blocks, x, stream) with x the [batch, rows, cols] bf16 result in the matrices' own
         # layout, after the GEMMs and before the update is applied (parity tests read it there)
         self.ns_output_hook = None
+        # nonzero: written to the Newton-Schulz GEMMs' stall-request word (status word 3) for the
+        # next steps, making that role's bounded wait expire (tests of the timeout path)
+        self.gemm_stall_request = 0
         # rebuild of batch i+1 on a side stream (one CTA per SM) while batch i is on the tensor
         # cores; off by default: the GEMMs already run at the power cap
         self.overlap = os.environ.get("MUZO_OVERLAP_REBUILD", "0") == "1"
@@ -435,6 +438,8 @@ class StepEngine:
         base = self.state.data_ptr()
         sums_ptr, flags_ptr, stats_ptr = base, base + self.flags_off, base + self.stats_off
         status_ptr = flags_ptr + 4 * (max(self.n_slots, 1))
+        if self.gemm_stall_request:
+            self.state.view(torch.int32)[(status_ptr - base) // 4 + 3] = int(self.gemm_stall_request)
         lr32 = float(np.float32(lr))
         decay = float(np.float32(1.0 - lr * opt.weight_decay))
         apply_decay = 1 if opt.weight_decay else 0
@@ -511,7 +516,9 @@ class StepEngine:
         s_flags = flags_ptr + 4 * ch.slot0
         s_stats = stats_ptr + 4 * _lib.NSTATS * ch.slot0
         self._mark("ns", True, stream)
-        parity = ns_iterations(ch.buf, n, opt.ns_steps, 0, status_ptr, sp)
+        # the last GEMM also sums U^2 per block and flags a non-finite result
+        parity = ns_iterations(ch.buf, n, opt.ns_steps, 0, status_ptr, sp, sums_ptr=s_sums,
+                               scales_ptr=ch.scales.data_ptr(), flags_ptr=s_flags)
         self._mark("ns", False, stream)
         if ch.pad_views is not None:
             with torch.cuda.stream(stream):
@@ -521,7 +528,8 @@ class StepEngine:
             self.ns_output_hook(ch.blocks, x, stream)
         table, items = ch.apply_tables[parity if ch.pad_views is None else 0]
         self._mark("apply", True, stream)
-        _lib.launch("muzo_update_sumsq", table.data_ptr(), n, items, ch.scales.data_ptr(), s_sums, s_flags, sp)
+        if opt.ns_steps <= 0:  # no GEMM: the normalised momentum itself is the update
+            _lib.launch("muzo_update_sumsq", table.data_ptr(), n, items, ch.scales.data_ptr(), s_sums, s_flags, sp)
         _lib.launch("muzo_apply_update", table.data_ptr(), n, items, ch.dtype_code, ch.scales.data_ptr(), lr32,
                     float(opt.update_ratio_clip), apply_decay, decay, s_sums, s_flags, s_stats, sp)
         self._mark("apply", False, stream)

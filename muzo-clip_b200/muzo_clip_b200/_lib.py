@@ -82,7 +82,7 @@ _SIGNATURES = {
     "muzo_ns_normalize": ([_vp, _i32, _i64, _vp, _vp, _vp], _i32),
     "muzo_ns_gemm": (
         [_vp, _i64, _i64, _i32, _vp, _i64, _i64, _i32, _vp, _i64, _i64, _vp, _i32, _f32, _f32,
-         _i64, _i64, _i64, _i64, _i32, _vp, _vp],
+         _i64, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _vp],
         _i32,
     ),
     "muzo_update_sumsq": ([_vp, _i32, _i64, _vp, _vp, _vp, _vp], _i32),

@@ -90,15 +90,19 @@ def allocate_ns_buffers(rows: int, cols: int, batch: int, device: torch.device) 
 
 
 def _gemm(a, lda, abs_, a_mn, b, ldb, bbs, b_mn, d, ldd, dbs, e, epi, c1, c2, m, n, k, batch,
-          status, stream, symmetric: int = 0) -> None:
+          status, stream, symmetric: int = 0, sums=None, scales=None, flags=None) -> None:
     _lib.launch("muzo_ns_gemm", a, lda, abs_, a_mn, b, ldb, bbs, b_mn, d, ldd, dbs, e, epi, float(c1), float(c2),
-                m, n, k, batch, symmetric, status, stream)
+                m, n, k, batch, symmetric, sums, scales, flags, status, stream)
 
 
 def ns_iterations(buf: NSBuffers, batch: int, steps: int, start_parity: int, status_ptr: int,
-                  stream: int, symmetric: int = 1) -> int:
+                  stream: int, symmetric: int = 1, sums_ptr: int | None = None, scales_ptr: int | None = None,
+                  flags_ptr: int | None = None) -> int:
     """Run ``steps`` quintic iterations on the first ``batch`` matrices; return the parity of the
-    buffer that holds the result."""
+    buffer that holds the result. With ``sums_ptr`` (and ``scales_ptr``, ``flags_ptr``) the last
+    iteration's update GEMM also accumulates each matrix's sum of (result * scale)^2 into its
+    MUZO_SUM_U2 slot and flags a non-finite result (what muzo_update_sumsq does in a pass of
+    its own)."""
 
     a_c, b_c, c_c = (np.float32(v) for v in NS_COEFFS)
     rows, cols, ld, ldm = buf.rows, buf.cols, buf.ld, buf.ldm
@@ -109,7 +113,9 @@ def ns_iterations(buf: NSBuffers, batch: int, steps: int, start_parity: int, sta
     pb = buf.b.data_ptr()
     tall = rows > cols
     parity = start_parity
-    for _ in range(int(steps)):
+    for it in range(int(steps)):
+        last = it + 1 == int(steps)
+        sums = (sums_ptr, scales_ptr, flags_ptr) if last and sums_ptr else (None, None, None)
         px = buf.x_slot(parity).data_ptr()
         py = buf.x_slot(parity ^ 1).data_ptr()
         # A = X X^T and B = b A + c A A are symmetric: only their upper-triangle tiles are
@@ -128,11 +134,11 @@ def ns_iterations(buf: NSBuffers, batch: int, steps: int, start_parity: int, sta
         if not tall:
             # X' = a X + B @ X: X[k][n] is N-contiguous
             _gemm(pb, ldm, m_bs, 0, px, ld, x_bs, 1, py, ld, x_bs, px, _lib.EPI_UPDATE, a_c, 0.0,
-                  m, cols, m, batch, status_ptr, stream)
+                  m, cols, m, batch, status_ptr, stream, 0, *sums)
         else:
             # G' = (a X + B X)^T = a G + G B^T: B's rows are K-contiguous
             _gemm(px, ld, x_bs, 0, pb, ldm, m_bs, 0, py, ld, x_bs, px, _lib.EPI_UPDATE, a_c, 0.0,
-                  rows, cols, cols, batch, status_ptr, stream)
+                  rows, cols, cols, batch, status_ptr, stream, 0, *sums)
         parity ^= 1
     return parity
 

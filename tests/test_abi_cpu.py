@@ -33,7 +33,7 @@ def test_python_binding_covers_header():
     from muzo_clip_b200 import _lib
 
     assert set(_declared_symbols()) == set(_lib.EXPORTED)
-    assert _lib.lib.muzo_abi_version() == 1
+    assert _lib.lib.muzo_abi_version() == 2
 
 
 def _header_constants() -> dict[str, int]:
@@ -115,9 +115,9 @@ def test_status_strings_and_bad_args():
     assert _lib.lib.muzo_status_string(3).startswith(b"pointer")
     # null tables are rejected before anything touches a device
     assert _lib.lib.muzo_perturb_segments(None, 1, 1024, None, 1, 0, 1.0, None) == 1
-    assert _lib.lib.muzo_ns_gemm(None, 8, 0, 0, None, 8, 0, 0, None, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None) == 1
+    assert _lib.lib.muzo_ns_gemm(None, 8, 0, 0, None, 8, 0, 0, None, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None, None, None, None) == 1
     # unaligned leading dimension
-    assert _lib.lib.muzo_ns_gemm(16, 12, 0, 0, 16, 8, 0, 0, 16, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None) == 3
+    assert _lib.lib.muzo_ns_gemm(16, 12, 0, 0, 16, 8, 0, 0, 16, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None, None, None, None) == 3
 
 
 # A fake, never-dereferenced device address: every call below is rejected by the library's host
@@ -163,12 +163,15 @@ _P = 256
     (lambda L: L.muzo_ns_normalize_noalloc((ctypes.c_void_p * 1)(), (ctypes.c_void_p * 1)(),
                                            (ctypes.c_int64 * 1)(), 1, 9, _P, None), 2),
     # Newton-Schulz GEMM: epilogue operand, epilogue code, symmetric shapes, leading dimensions
-    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 1, 1.0, 1.0, 8, 8, 8, 1, 0, None, None), 1),
-    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 3, 1.0, 1.0, 8, 8, 8, 1, 0, None, None), 1),
-    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 16, 0, None, 0, 0.0, 0.0, 8, 16, 8, 1, 1, None, None), 1),
-    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 2, 1.0, 0.0, 8, 8, 8, 1, 1, None, None), 1),
-    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 16, 1, 0, None, None), 1),
-    (lambda L: L.muzo_ns_gemm(_P + 8, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None), 3),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 1, 1.0, 1.0, 8, 8, 8, 1, 0, None, None, None, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 3, 1.0, 1.0, 8, 8, 8, 1, 0, None, None, None, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 16, 0, None, 0, 0.0, 0.0, 8, 16, 8, 1, 1, None, None, None, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 2, 1.0, 0.0, 8, 8, 8, 1, 1, None, None, None, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 16, 1, 0, None, None, None, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P + 8, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None, None, None, None), 3),
+    # sums of squares only with the update epilogue, and then with scales and flags
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 1, 1.0, 1.0, 8, 8, 8, 1, 0, _P, _P, _P, None, None), 1),
+    (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 2, 1.0, 0.0, 8, 8, 8, 1, 0, _P, None, _P, None, None), 1),
     # QK-Clip
     (lambda L: L.muzo_qk_max(None, _P, 1, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 1),
     (lambda L: L.muzo_qk_max(_P, _P, 1, 1, 8, 3, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 1),  # GQA

@@ -249,7 +249,8 @@ def _gemm_case(device, m, n, k, batch, a_mn, b_mn, epi):
     lda, ldb, ldd = A_st.shape[-1], B_st.shape[-1], D.shape[-1]
     L.check(L.lib.muzo_ns_gemm(A_st.data_ptr(), lda, A_st[0].numel(), a_mn, B_st.data_ptr(), ldb, B_st[0].numel(), b_mn,
                                D.data_ptr(), ldd, D[0].numel(), E.data_ptr() if epi else None, epi, float(c1),
-                               float(c2), m, n, k, batch, 0, status.data_ptr(), L.stream_ptr(device)), "gemm")
+                               float(c2), m, n, k, batch, 0, None, None, None, status.data_ptr(),
+                               L.stream_ptr(device)), "gemm")
     torch.cuda.synchronize()
     assert status.tolist() == [0, 0, 0, 0]  # no wait expired; scheduler counters rewound
     acc = torch.matmul(A_log.float(), B_log.float())
@@ -320,10 +321,10 @@ def test_ns_gemm_symmetric_outputs(device, gemm_kernel, m, k, batch, tall):
         A = torch.zeros((batch, m, ld), dtype=torch.bfloat16, device=device)
         B = torch.zeros_like(A)
         L.check(L.lib.muzo_ns_gemm(*a_args, A.data_ptr(), ld, m * ld, None, L.EPI_STORE, 0.0, 0.0, m, m, k, batch,
-                                   sym, status.data_ptr(), L.stream_ptr(device)), "xxt")
+                                   sym, None, None, None, status.data_ptr(), L.stream_ptr(device)), "xxt")
         L.check(L.lib.muzo_ns_gemm(A.data_ptr(), ld, m * ld, 0, A.data_ptr(), ld, m * ld, 1, B.data_ptr(), ld,
                                    m * ld, A.data_ptr(), L.EPI_POLY, -4.775, 2.0315, m, m, m, batch, sym,
-                                   status.data_ptr(), L.stream_ptr(device)), "poly")
+                                   None, None, None, status.data_ptr(), L.stream_ptr(device)), "poly")
         torch.cuda.synchronize()
         outs[sym] = (A[..., :m].float().cpu(), B[..., :m].float().cpu())
     assert status.tolist() == [0, 0, 0, 0]  # no wait expired; scheduler counters rewound
