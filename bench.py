@@ -3,7 +3,10 @@
 One step = the optimizer share of ``estimate_projection`` (three perturbation passes: +eps,
 -2eps, +eps, over every selected matrix; the loss closure returns synthetic scalars, no model
 forward) followed by ``step()`` (H=8 momentum rebuild, Newton-Schulz, scaled/clipped update with
-weight decay) through the public MuZOClipOptimizer API.
+weight decay) through the public MuZOClipOptimizer API. The history is filled by H projections
+before the warm-up, as in a running job. The line reports the optimizer with noise_cache=True
+(each projection's rounded noise kept on the device, bit-identical results); the default
+configuration, which regenerates all noise, is timed in the same run under "variants".
 
 Workload: 32 layers x {q 4096x4096, k 1024x4096, v 1024x4096, o 4096x4096, gate 14336x4096,
 up 14336x4096, down 4096x14336}, bf16 N(0, 0.02) weights, horizon 8, beta 0.9, p ~ N(0,1) clipped
@@ -21,6 +24,7 @@ extrapolated to the full step.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -210,19 +214,13 @@ def setup_dist():
     return None, 0, 1, local
 
 
-def run_gpu(args) -> int:
-    dist, rank, world, local = setup_dist()
-    device = torch.device("cuda", local)
-    from muzo_clip_b200 import MuZOClipOptimizer, _lib
-    from muzo_clip_b200.muzo_optimizer import HistoryItem
+def _time_steps(opt, args, device, dist, local) -> dict:
+    """Fill the history through H projections and steps, run W warm-up steps, then time exactly K
+    steps (estimate_projection + step) with CUDA events on the launching stream between a barrier
+    and a synchronize on both sides, max over ranks; per-phase device time from CUDA events, wall
+    time through the public API, nvidia-smi clocks sampled during the timed steps."""
+    from muzo_clip_b200 import _lib
 
-    model = Llama8BMatrices(device, layers=args.layers)
-    pg = dist.group.WORLD if dist is not None else None
-    opt = MuZOClipOptimizer(model, horizon=HORIZON, min_history=4, beta_momentum=0.9, lr=1e-5, seed=1234,
-                            process_group=pg, noise_cache=args.noise_cache)
-    rng = random.Random(99)
-    for _ in range(HORIZON):
-        opt.history.append(HistoryItem(rng.randrange(0, 2**63 - 1), max(-3.0, min(3.0, rng.gauss(0, 1))), 0.0, 0.0, 0.0))
     loss_rng = random.Random(7)
 
     def closure():
@@ -232,19 +230,19 @@ def run_gpu(args) -> int:
         opt.estimate_projection(closure)
         return opt.step()
 
-    stream = torch.cuda.current_stream(device)
+    # optimizer state of a running job: a full history, each entry made by a projection
+    for _ in range(HORIZON):
+        one_step()
     for _ in range(args.warmup):
         st = one_step()
         assert not st["skipped"], st
-    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
 
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # timed region: device time by CUDA events on the launching stream (per phase as well),
-    # wall time through the public API
     engine = opt._engine
     barrier()
     launches0 = _lib.launch_count
@@ -267,10 +265,50 @@ def run_gpu(args) -> int:
         t = torch.tensor([dev_ms, wall_ms], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms, wall_ms = t.tolist()
+    return {"dev_ms": dev_ms, "wall_ms": wall_ms, "phases": phases, "launches": launches, "clocks": clocks.summary(),
+            "kept_entries": engine.kept_entries, "noise_slots": len(engine.slot_seed),
+            "keep_noise": bool(engine.keep_noise)}
 
+
+def run_gpu(args) -> int:
+    dist, rank, world, local = setup_dist()
+    device = torch.device("cuda", local)
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    model = Llama8BMatrices(device, layers=args.layers)
+    pg = dist.group.WORLD if dist is not None else None
+
+    def make(noise_cache):
+        return MuZOClipOptimizer(model, horizon=HORIZON, min_history=4, beta_momentum=0.9, lr=1e-5, seed=1234,
+                                 process_group=pg, noise_cache=noise_cache)
+
+    # the configuration the line reports (the noise of the current projection and of every
+    # history entry kept in device memory; bit-identical results), then, as a variant, the
+    # optimizer's default configuration (every pass and the rebuild regenerate the noise)
+    opt = make(not args.no_noise_cache)
+    run = _time_steps(opt, args, device, dist, local)
+    engine = opt._engine
+    phases, dev_ms, wall_ms = run["phases"], run["dev_ms"], run["wall_ms"]
+    variant = None
+    if not args.no_variant and not args.no_noise_cache:
+        noise_pool = engine.noise_pool
+        engine.noise_pool = None
+        del noise_pool
+        torch.cuda.empty_cache()
+        plain = make(False)
+        variant = _time_steps(plain, args, device, dist, local)
+        del plain
+        gc.collect()    # the optimizer and its engine reference each other
+        torch.cuda.empty_cache()
+
+    n_elems = total_numel(args.layers)
+    kept = run["keep_noise"] and run["kept_entries"] == HORIZON
     perturb_ms = phases.get("perturb", 0.0) / 3.0          # three passes per step
-    perturb_bytes = 4.0 * total_numel(args.layers)
+    perturb_bytes = 4.0 * n_elems                          # per pass, algorithmic
     perturb_gbs = perturb_bytes / (perturb_ms * 1e-3) / 1e9 if perturb_ms > 0 else 0.0
+    # moved per step by the three passes: W read and written each pass, plus the noise written
+    # once and read twice when it is kept
+    perturb_moved = (3 * 4.0 + (3 * 2.0 if run["keep_noise"] else 0.0)) * n_elems
     ns_ms = phases.get("ns", 0.0)
     ns_flops = engine.owned_ns_flops()
     ns_exec = engine.owned_ns_flops_executed()
@@ -279,6 +317,9 @@ def run_gpu(args) -> int:
 
     # Rademacher perturbation bandwidth (untimed, after the timed region): one pass over the
     # same matrices through an optimizer configured for Rademacher noise
+    del opt
+    gc.collect()
+    torch.cuda.empty_cache()
     rad = MuZOClipOptimizer(model, distribution="rademacher", seed=4321)
     rad_engine = rad._engine_for_step()
     for _ in range(3):
@@ -293,19 +334,38 @@ def run_gpu(args) -> int:
 
     if rank == 0:
         peaks = load_peaks()
-        clk = clocks.summary()
-        n_elems = total_numel(args.layers)
+        hbm = peaks["hbm_gbs"]
         ns_bytes_min = sum(ns_operand_bytes(b.rows, b.cols) for b in engine.owned)
         owned_elems = sum(b.rows * b.cols for b in engine.owned)
         rebuild_ms = max(phases.get("rebuild", 0.0), 1e-9)
-        rebuild_samples = float(HORIZON) * owned_elems
-        rebuild_bytes = 4.0 * owned_elems
+        rebuild_bytes = 4.0 * owned_elems                  # bf16(M) written, W read
         apply_ms = max(phases.get("apply", 0.0), 1e-9)
         apply_bytes = 6.0 * owned_elems        # update read (bf16), W read, W written
         norm_ms = max(phases.get("normalize", 0.0), 1e-9)
         norm_bytes = 4.0 * owned_elems         # bf16 momentum read and written
-        h2d = 8 * len(engine.blocks) * 3 + 8 * len(engine.owned) * HORIZON + 4 * HORIZON
+        h2d = 8 * len(engine.blocks) * 3 + 8 * len(engine.owned) * HORIZON + 12 * HORIZON
         d2h = engine.state_bytes + 16
+
+        def gbs(nbytes, ms):
+            return round(nbytes / (ms * 1e-3) / 1e9, 1)
+
+        if kept:
+            # every history entry read from its kept noise: H bf16 reads, W read, bf16(M) written
+            moved = (2.0 * HORIZON + 4.0) * owned_elems
+            rebuild_roofline = {
+                "bound": "hbm", "kernel": "rebuild_kept_linear_kernel", "achieved": gbs(moved, rebuild_ms),
+                "unit": "GB/s", "peak": hbm, "frac": round(gbs(moved, rebuild_ms) / hbm, 4),
+                "bytes": moved, "bytes_note": "2H + 4 B per weight actually moved (H kept noise entries read)",
+                "algorithmic_bytes": rebuild_bytes, "algorithmic_achieved": gbs(rebuild_bytes, rebuild_ms),
+                "algorithmic_frac": round(gbs(rebuild_bytes, rebuild_ms) / hbm, 4)}
+        else:
+            # the rebuild regenerates H normal samples per weight: bound by the instruction issue
+            # rate (ncu: 43 instructions per sample, 74 % issue utilisation), not by HBM
+            rebuild_roofline = {
+                "bound": "issue", "kernel": "rebuild_kernel",
+                "achieved": round(float(HORIZON) * owned_elems / (rebuild_ms * 1e-3) / 1e9, 1),
+                "unit": "G normal samples/s", "hbm_achieved": gbs(rebuild_bytes, rebuild_ms),
+                "hbm_frac": round(gbs(rebuild_bytes, rebuild_ms) / hbm, 4), "algorithmic_bytes": rebuild_bytes}
         line = {
             "metric": METRIC,
             "value": round(dev_ms, 3),
@@ -322,7 +382,9 @@ def run_gpu(args) -> int:
             "config": {"workload": WORKLOAD, "layers": args.layers, "matrices": len(engine.blocks),
                        "elements": n_elems, "horizon": HORIZON, "ns_steps": 5, "distribution": "normal",
                        "parallelism": f"replica perturb + NS partition x{world}",
-                       "noise_cache": bool(engine.keep_noise),
+                       "noise_cache": run["keep_noise"], "noise_slots": run["noise_slots"],
+                       "kept_history_entries": run["kept_entries"],
+                       "history": f"filled by {HORIZON} projections before the warm-up",
                        "l2": "inputs larger than L2 (14 GB of weights per pass)"},
             "perturb_gbs": round(perturb_gbs, 1),
             "perturb_ms": round(perturb_ms, 3),
@@ -347,40 +409,41 @@ def run_gpu(args) -> int:
                 "operand_bytes": round(ns_bytes_min),
             },
             "perturb_roofline": {
-                "bound": "hbm", "achieved": round(perturb_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(perturb_gbs / peaks["hbm_gbs"], 4), "peak_source": f"{peaks['source']} copy",
-                "rademacher_achieved": round(rad_gbs, 1), "rademacher_frac": round(rad_gbs / peaks["hbm_gbs"], 4),
-                "traffic": PERTURB_DRAM_BYTES_PER_PASS, "traffic_unit": "DRAM bytes per pass",
+                "bound": "hbm", "achieved": round(perturb_gbs, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(perturb_gbs / hbm, 4), "peak_source": f"{peaks['source']} copy",
+                "achieved_note": "4 B per weight and pass (W read + written) over the mean pass time",
+                "moved_gbs": gbs(perturb_moved, 3.0 * perturb_ms),
+                "moved_frac": round(gbs(perturb_moved, 3.0 * perturb_ms) / hbm, 4),
+                "rademacher_achieved": round(rad_gbs, 1), "rademacher_frac": round(rad_gbs / hbm, 4),
+                "traffic": PERTURB_DRAM_BYTES_PER_PASS, "traffic_unit": "DRAM bytes per regenerating pass",
                 "traffic_source": TRAFFIC_SOURCE, "algorithmic_bytes": perturb_bytes,
             },
-            # the rebuild regenerates H normal samples per weight: its bound is the instruction
-            # issue rate (ncu: 43 instructions per sample, 74 % issue utilisation), not HBM
-            "rebuild_roofline": {
-                "bound": "issue", "achieved": round(rebuild_samples / (rebuild_ms * 1e-3) / 1e9, 1),
-                "unit": "G normal samples/s", "hbm_achieved": round(rebuild_bytes / (rebuild_ms * 1e-3) / 1e9, 1),
-                "hbm_frac": round(rebuild_bytes / (rebuild_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
-                "algorithmic_bytes": rebuild_bytes,
-            },
+            "rebuild_roofline": rebuild_roofline,
             # the apply (update and W read, W written: 6 B per owned weight; the update's sum of
             # squares comes from the last Newton-Schulz GEMM's epilogue) and, separately, the
             # normalisation of the rebuilt momentum (4 B per owned weight)
             "update_roofline": {
-                "bound": "hbm", "kernel": "apply_update_kernel",
-                "achieved": round(apply_bytes / (apply_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "peak": peaks["hbm_gbs"], "frac": round(apply_bytes / (apply_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                "bound": "hbm", "kernel": "apply_update_kernel", "achieved": gbs(apply_bytes, apply_ms),
+                "unit": "GB/s", "peak": hbm, "frac": round(gbs(apply_bytes, apply_ms) / hbm, 4),
                 "algorithmic_bytes": apply_bytes,
             },
             "normalize_roofline": {
-                "bound": "hbm", "kernel": "ns_normalize_kernel",
-                "achieved": round(norm_bytes / (norm_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "peak": peaks["hbm_gbs"], "frac": round(norm_bytes / (norm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                "bound": "hbm", "kernel": "ns_normalize_kernel", "achieved": gbs(norm_bytes, norm_ms),
+                "unit": "GB/s", "peak": hbm, "frac": round(gbs(norm_bytes, norm_ms) / hbm, 4),
                 "algorithmic_bytes": norm_bytes,
             },
             "e2e": {"value": round(wall_ms, 3), "unit": "ms/step", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": int(launches),
-            "clocks": clk,
+            "gpu_launches": int(run["launches"]),
+            "clocks": run["clocks"],
         }
+        if variant is not None:
+            line["variants"] = {"regenerated_noise": {
+                "note": "the optimizer's default configuration (noise_cache=False): every pass and history entry "
+                        "regenerated from its seed; same workload, timed in this run after the line's own steps",
+                "ms_per_step": round(variant["dev_ms"], 3), "e2e_ms_per_step": round(variant["wall_ms"], 3),
+                "phase_ms": {k: round(v, 3) for k, v in variant["phases"].items()},
+                "gpu_launches": int(variant["launches"]), "clocks": variant["clocks"]}}
         if world == 1 and not args.no_cpu_baseline:
             cpu_ms, sample, cores = cpu_sample_ms()
             line["cpu_baseline"] = {"value": round(cpu_ms, 1), "unit": "ms/step", "cores": cores, "kind": "port",
@@ -597,8 +660,10 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--keep", action="store_true",
                     help="perturb case: time a pass that reads kept noise (muzo_perturb_kept_noise)")
-    ap.add_argument("--noise-cache", action="store_true",
-                    help="keep each projection's noise between its passes (MuZOClipOptimizer(noise_cache=True))")
+    ap.add_argument("--no-noise-cache", action="store_true",
+                    help="time only the default configuration (every pass and history entry regenerates its noise)")
+    ap.add_argument("--no-variant", action="store_true",
+                    help="skip the regenerated-noise variant timed before the kept-noise line")
     ap.add_argument("--sweep", action="store_true",
                     help="with --case: ns = 5 shapes x batch 8; perturb = 1 M..2 G elements; rebuild = horizon 1..16")
     args = ap.parse_args()

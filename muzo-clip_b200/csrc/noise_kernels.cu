@@ -441,6 +441,195 @@ __device__ __forceinline__ void rebuild_chunk(const muzo_segment* __restrict__ s
   if (!finite) atomicOr(flags + sv.block, MUZO_FLAG_NONFINITE_INPUT);
 }
 
+// M of the history rebuild in which history entry h is read from slot_base[h] + segs[i].kept
+// (the block's byte offset inside a slot, in the block's dtype and layout) when slot_base[h] is
+// nonzero and regenerated otherwise; the same arithmetic, in the same order, as rebuild_chunk.
+template <int PDTYPE>
+__device__ __forceinline__ void rebuild_history_chunk(const muzo_segment* __restrict__ segs, int nsegs,
+                                                      const uint64_t* __restrict__ keys,
+                                                      const float* __restrict__ alphas,
+                                                      const uint64_t* __restrict__ slot_base, int horizon,
+                                                      int normalize, float inv_coeff_sum, double* __restrict__ sums,
+                                                      int32_t* __restrict__ flags, int64_t chunk) {
+  const int64_t item0 = chunk * MUZO_ITEMS_PER_CTA;
+  const muzo_segment& g = segs[find_segment(segs, nsegs, item0)];
+  const SegView sv = cta_segment(segs, nsegs, PDTYPE, MUZO_BF16, chunk);
+  const uint64_t kept_off = reinterpret_cast<uint64_t>(g.kept) + static_cast<uint64_t>(g.elem_start) * elem_size(PDTYPE);
+  const uint32_t octets = sv.threads / 8;
+  const bool vec = vec_ok(sv.out, 0, MUZO_BF16) && vec_ok(sv.param, 0, PDTYPE);
+  const uint64_t* bkeys = keys + static_cast<int64_t>(sv.block) * horizon;
+  const int half = threadIdx.x & 1;
+  const int slot = threadIdx.x >> 1;
+  double m2 = 0.0, x2 = 0.0, w2 = 0.0;
+  bool finite = true;
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const uint32_t local = static_cast<uint32_t>(sv.local_item0) + it * kElemThreads + slot;
+    const uint32_t trip = local / octets;
+    const uint32_t oct = local - trip * octets;
+    const int64_t li0 = static_cast<int64_t>(sv.threads) * (4ll * trip) + 8ll * oct + 4 * half;
+    if (li0 >= sv.numel) continue;
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[j][k] = 0.0f;
+#pragma unroll 1
+    for (int h = 0; h < horizon; ++h) {
+      const uint64_t base = slot_base[h];
+      if (base != 0) {
+        const char* kp = reinterpret_cast<const char*>(base + kept_off);
+        accumulate_kept4x4<PDTYPE>(kp, li0, sv.threads, sv.numel, vec_ok(kp, 0, PDTYPE), alphas[h], acc);
+      } else {
+        accumulate4x4<MUZO_NORMAL, PDTYPE>(bkeys[h], 8ull * oct + 4 * half, sv.philox_offset, trip, alphas[h], acc);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t li = li0 + static_cast<int64_t>(sv.threads) * j;
+      if (li >= sv.numel) break;
+      float m[4], w[4];
+      const int cnt = li + 4 <= sv.numel ? 4 : static_cast<int>(sv.numel - li);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m[k] = normalize ? acc[j][k] * inv_coeff_sum : acc[j][k];
+      if (vec && cnt == 4) {
+        load4(sv.param, li, PDTYPE, w);
+        store4_bf16(sv.out, li, m);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[k] = k < cnt ? load_elem(sv.param, li + k, PDTYPE) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (k < cnt) store_elem(sv.out, li + k, MUZO_BF16, m[k]);
+      }
+      float pm = 0.0f, px = 0.0f, pw = 0.0f;
+      float mb[4] = {m[0], m[1], m[2], m[3]};
+      bf16r2(mb[0], mb[1]);
+      bf16r2(mb[2], mb[3]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (k < cnt) {
+          finite = finite && isfinite(m[k]);
+          pm = __fmaf_rn(m[k], m[k], pm);
+          px = __fmaf_rn(mb[k], mb[k], px);
+          pw = __fmaf_rn(w[k], w[k], pw);
+        }
+      }
+      m2 += pm; x2 += px; w2 += pw;
+    }
+  }
+  double* bs = sums + static_cast<int64_t>(sv.block) * MUZO_NSUMS;
+  block_accumulate3<kRebuildThreads>(m2, x2, w2, bs + MUZO_SUM_M2, bs + MUZO_SUM_X2, bs + MUZO_SUM_W2);
+  if (!finite) atomicOr(flags + sv.block, MUZO_FLAG_NONFINITE_INPUT);
+}
+
+template <int PDTYPE>
+__global__ void __launch_bounds__(kRebuildThreads, 2)
+rebuild_history_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
+                       const float* __restrict__ alphas, const uint64_t* __restrict__ slot_base, int horizon,
+                       int normalize, float inv_coeff_sum, double* __restrict__ sums, int32_t* __restrict__ flags,
+                       int64_t nchunks) {
+  for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x)
+    rebuild_history_chunk<PDTYPE>(segs, nsegs, keys, alphas, slot_base, horizon, normalize, inv_coeff_sum, sums,
+                                  flags, chunk);
+}
+
+// The rebuild when every history entry is kept: a plain stream over linear segments (param = the
+// block, out = bf16(M), kept = the block's byte offset inside a slot). Per 8 elements it reads
+// the H kept vectors and the weights and writes bf16(M): 2H + 4 bytes per element for 16-bit
+// weights. Accumulation order and arithmetic are rebuild_chunk's: acc = fma(alpha_h, z_h, acc)
+// for h = 0 (newest) .. H-1, then the normalisation multiply.
+constexpr int kKeptLoadsInFlight = 4;
+
+template <int PDTYPE>
+__global__ void __launch_bounds__(kElemThreads)
+rebuild_kept_linear_kernel(const muzo_segment* __restrict__ segs, int nsegs, const float* __restrict__ alphas,
+                           const uint64_t* __restrict__ slot_base, int horizon, int normalize, float inv_coeff_sum,
+                           double* __restrict__ sums, int32_t* __restrict__ flags) {
+  const int64_t item0 = static_cast<int64_t>(blockIdx.x) * MUZO_ITEMS_PER_CTA;
+  const muzo_segment& g = segs[find_segment(segs, nsegs, item0)];
+  const char* param = static_cast<const char*>(g.param);
+  char* out = static_cast<char*>(g.out);
+  const uint64_t kept_off = reinterpret_cast<uint64_t>(g.kept);
+  const int64_t numel = g.numel;
+  const int64_t local_item0 = item0 - g.item_begin;
+  const bool vec = vec_ok(out, 0, MUZO_BF16) && vec_ok(param, 0, PDTYPE) && (kept_off & 15u) == 0;
+  double m2 = 0.0, x2 = 0.0, w2 = 0.0;
+  bool finite = true;
+#pragma unroll 1
+  for (int it = 0; it < kItemsPerThread; ++it) {
+    const int64_t li = (local_item0 + it * kElemThreads + threadIdx.x) * 8;
+    if (li >= numel) break;
+    const int cnt = li + 8 <= numel ? 8 : static_cast<int>(numel - li);
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
+    if (vec && cnt == 8) {
+      // loads of several entries go out before their multiply-adds (memory-level parallelism)
+#pragma unroll 1
+      for (int h0 = 0; h0 < horizon; h0 += kKeptLoadsInFlight) {
+        Packed8<PDTYPE> z[kKeptLoadsInFlight];
+#pragma unroll
+        for (int q = 0; q < kKeptLoadsInFlight; ++q)
+          if (h0 + q < horizon) z[q].load(reinterpret_cast<const char*>(slot_base[h0 + q] + kept_off), li);
+#pragma unroll
+        for (int q = 0; q < kKeptLoadsInFlight; ++q) {
+          if (h0 + q < horizon) {
+            float v[8];
+            z[q].unpack(v);
+            const float a = alphas[h0 + q];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[k] = __fmaf_rn(a, v[k], acc[k]);
+          }
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int h = 0; h < horizon; ++h) {
+        const char* kp = reinterpret_cast<const char*>(slot_base[h] + kept_off);
+        const float a = alphas[h];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k < cnt) acc[k] = __fmaf_rn(a, load_elem(kp, li + k, PDTYPE), acc[k]);
+      }
+    }
+    float m[8], w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m[k] = normalize ? acc[k] * inv_coeff_sum : acc[k];
+    if (vec && cnt == 8) {
+      load8(param, li, PDTYPE, w);
+      store8(out, li, MUZO_BF16, m);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) w[k] = k < cnt ? load_elem(param, li + k, PDTYPE) : 0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < cnt) store_elem(out, li + k, MUZO_BF16, m[k]);
+    }
+    // the sums in the rebuild kernel's grouping: fp32 chains over 4 elements, added in fp64
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      float pm = 0.0f, px = 0.0f, pw = 0.0f;
+      float mb[4] = {m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3]};
+      bf16r2(mb[0], mb[1]);
+      bf16r2(mb[2], mb[3]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (4 * q + k < cnt) {
+          finite = finite && isfinite(m[4 * q + k]);
+          pm = __fmaf_rn(m[4 * q + k], m[4 * q + k], pm);
+          px = __fmaf_rn(mb[k], mb[k], px);
+          pw = __fmaf_rn(w[4 * q + k], w[4 * q + k], pw);
+        }
+      }
+      m2 += pm; x2 += px; w2 += pw;
+    }
+  }
+  double* bs = sums + static_cast<int64_t>(g.block_index) * MUZO_NSUMS;
+  block_accumulate3<kElemThreads>(m2, x2, w2, bs + MUZO_SUM_M2, bs + MUZO_SUM_X2, bs + MUZO_SUM_W2);
+  if (!finite) atomicOr(flags + g.block_index, MUZO_FLAG_NONFINITE_INPUT);
+}
+
 template <int DIST, int PDTYPE, bool KEPT = false>
 __global__ void __launch_bounds__(kRebuildThreads, 2)
 rebuild_kernel(const muzo_segment* __restrict__ segs, int nsegs, const uint64_t* __restrict__ keys,
@@ -548,6 +737,49 @@ int muzo_rebuild_segments_kept(const muzo_segment* d_segs, int nsegs, int64_t to
     constexpr int D = decltype(d)::value;
     rebuild_kernel<MUZO_NORMAL, D, true><<<grid, kRebuildThreads, 0, s>>>(
         d_segs, nsegs, d_keys, d_alphas, horizon, normalize, inv_coeff_sum, d_sums, d_flags, nchunks);
+  });
+  if (st != MUZO_OK) return st;
+  return launch_status();
+}
+
+int muzo_rebuild_segments_history(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                                  const uint64_t* d_keys, const float* d_alphas, const uint64_t* d_slot_base,
+                                  int horizon, int param_dtype, int normalize, float inv_coeff_sum,
+                                  double* d_sums, int32_t* d_flags, int max_ctas, void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_table(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_keys == nullptr || d_alphas == nullptr || d_slot_base == nullptr || d_sums == nullptr ||
+      d_flags == nullptr || horizon <= 0)
+    return MUZO_ERR_ARG;
+  const int64_t nchunks = total_items / MUZO_ITEMS_PER_CTA;
+  const int64_t ctas = (max_ctas > 0 && max_ctas < nchunks) ? max_ctas : nchunks;
+  const dim3 grid(static_cast<unsigned>(ctas));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dispatch_dtype(param_dtype, [&](auto d) {
+    constexpr int D = decltype(d)::value;
+    rebuild_history_kernel<D><<<grid, kRebuildThreads, 0, s>>>(d_segs, nsegs, d_keys, d_alphas, d_slot_base, horizon,
+                                                              normalize, inv_coeff_sum, d_sums, d_flags, nchunks);
+  });
+  if (st != MUZO_OK) return st;
+  return launch_status();
+}
+
+int muzo_rebuild_kept_linear(const muzo_segment* d_segs, int nsegs, int64_t total_items,
+                             const float* d_alphas, const uint64_t* d_slot_base, int horizon, int param_dtype,
+                             int normalize, float inv_coeff_sum, double* d_sums, int32_t* d_flags,
+                             void* stream) {
+  if (nsegs == 0 || total_items == 0) return MUZO_OK;
+  int st = check_table(d_segs, nsegs, total_items);
+  if (st != MUZO_OK) return st;
+  if (d_alphas == nullptr || d_slot_base == nullptr || d_sums == nullptr || d_flags == nullptr || horizon <= 0)
+    return MUZO_ERR_ARG;
+  const dim3 grid(static_cast<unsigned>(total_items / MUZO_ITEMS_PER_CTA));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  st = dispatch_dtype(param_dtype, [&](auto d) {
+    constexpr int D = decltype(d)::value;
+    rebuild_kept_linear_kernel<D><<<grid, kElemThreads, 0, s>>>(d_segs, nsegs, d_alphas, d_slot_base, horizon,
+                                                               normalize, inv_coeff_sum, d_sums, d_flags);
   });
   if (st != MUZO_OK) return st;
   return launch_status();

@@ -52,15 +52,11 @@ class PerturbGroup:
     table: torch.Tensor
     nsegs: int
     total_items: int
-    # kept noise: the first pass of a seed stores dtype(Z) (keep_*: noise segments whose out is
-    # the block's slot of the noise buffer), later passes of that seed read it back (kept_*:
-    # linear segments, param = block, out = its noise)
-    keep_table: torch.Tensor | None = None
-    keep_nsegs: int = 0
-    keep_items: int = 0
-    kept_table: torch.Tensor | None = None
-    kept_nsegs: int = 0
-    kept_items: int = 0
+    # kept noise, per slot of the noise pool: the first pass of a seed stores dtype(Z) (keep:
+    # noise segments whose out is the block's place in the slot), later passes of that seed read
+    # it back (kept: linear segments, param = block, out = its noise); (table, nsegs, items)
+    keep_tables: dict[int, tuple[torch.Tensor, int, int]] = field(default_factory=dict)
+    kept_tables: dict[int, tuple[torch.Tensor, int, int]] = field(default_factory=dict)
 
 
 @dataclass
@@ -75,6 +71,10 @@ class Chunk:
     rebuild_items: int
     norm_table: torch.Tensor
     norm_items: int
+    # every history entry kept: linear segments (param = block, out = bf16(M), kept = the block's
+    # byte offset in a noise slot)
+    kept_rebuild_table: torch.Tensor | None = None
+    kept_rebuild_items: int = 0
     apply_tables: dict[int, tuple[torch.Tensor, int]] = field(default_factory=dict)  # by parity
     scales: torch.Tensor | None = None
     pad_views: list[torch.Tensor] | None = None
@@ -152,13 +152,16 @@ class StepEngine:
         self.dist = _lib.dist_code(opt.distribution)
         self.sms, self.max_thr = _lib.device_geometry(self.device)
         self._key_cache: dict[int, np.ndarray] = {}
-        # noise kept between the passes of one projection (normal noise only: Rademacher passes
-        # are already close to the HBM rate)
+        # kept noise (normal noise only: Rademacher passes are close to the HBM rate already): a
+        # pool of slots, each holding one projection's rounded noise for every block, so that the
+        # later passes of a projection and the rebuild of every history entry that still has a
+        # slot read the noise instead of regenerating it
         self.keep_noise = bool(getattr(opt, "noise_cache", False)) and self.dist == _lib.NORMAL
-        self.noise_buffer: torch.Tensor | None = None
+        self.noise_pool: torch.Tensor | None = None
+        self.slot_bytes = 0
+        self.slot_seed: list[int | None] = []
         self._noise_offsets: list[int] = []
-        self._kept_seed: int | None = None
-        self._rebuild_kept = False
+        self.kept_entries = 0     # history entries the last rebuild read from kept noise
         self._build_perturb_groups()
         costs = [ns_flops(b.rows, b.cols, max(opt.ns_steps, 1)) for b in blocks]
         self.owner = partition_blocks(costs, world) if world > 1 else [0] * len(blocks)
@@ -176,7 +179,7 @@ class StepEngine:
         # cores; off by default: the GEMMs already run at the power cap
         self.overlap = os.environ.get("MUZO_OVERLAP_REBUILD", "0") == "1"
         horizon = max(opt.horizon, 1)
-        self.uploader = _Uploader(self.device, 8 * (len(blocks) * (horizon + 1) + 64))
+        self.uploader = _Uploader(self.device, 8 * (len(blocks) * (horizon + 1) + 2 * horizon + 64))
 
     # ------------------------------------------------------------------ bookkeeping
     @staticmethod
@@ -212,50 +215,95 @@ class StepEngine:
         if self.keep_noise:
             self._build_noise_buffer()
 
+    NOISE_POOL_RESERVE = 24 << 30   # device memory left free for the workspace and the rest
+
     def _build_noise_buffer(self) -> None:
-        """One device buffer for the rounded noise of every block (the block's dtype and layout,
-        256-byte aligned slots) and the two tables per group that write and read it. Left out,
-        with a warning, when it would take more than half of the free device memory."""
+        """The noise pool: up to horizon + 1 slots (the projection being evaluated and every
+        history entry), each one buffer of the rounded noise of every block in the block's dtype
+        and layout (256-byte aligned places), as many as fit next to 24 GiB left free (at most
+        MUZO_NOISE_SLOTS). Left out, with a warning, when not even one slot fits."""
         offsets, total = [], 0
         for b in self.blocks:
             offsets.append(total)
             total += (b.numel * b.tensor.element_size() + 255) // 256 * 256
+        total = max(total, 256)
         free, _ = torch.cuda.mem_get_info(self.device)
-        if total > free // 2:
-            logger.warning("noise_cache needs %.1f GB of device memory, more than half of the %.1f GB free; "
+        want = max(int(self.opt.horizon), 1) + 1
+        cap = os.environ.get("MUZO_NOISE_SLOTS")
+        if cap:
+            want = min(want, max(int(cap), 0))
+        fit = max(0, (free - self.NOISE_POOL_RESERVE) // total)
+        if fit == 0 and total <= free // 2:   # small devices: one slot, at most half the free memory
+            fit = 1
+        nslots = int(min(want, fit))
+        if nslots < 1:
+            logger.warning("noise_cache needs %.1f GB of device memory per projection, more than is free (%.1f GB); "
                            "every pass regenerates its noise instead", total / 1e9, free / 1e9)
             self.keep_noise = False
             return
-        self.noise_buffer = torch.empty(max(total, 256), dtype=torch.uint8, device=self.device)
+        self.noise_pool = torch.empty(nslots * total, dtype=torch.uint8, device=self.device)
+        self.slot_bytes = total
+        self.slot_seed = [None] * nslots
         self._noise_offsets = offsets
-        base = self.noise_buffer.data_ptr()
-        for g in self.perturb_groups:
+
+    def slot_base(self, slot: int) -> int:
+        return self.noise_pool.data_ptr() + slot * self.slot_bytes
+
+    def _slot_tables(self, g: PerturbGroup, slot: int):
+        """(keep, kept) tables of a perturbation group for one slot, built on first use."""
+        if slot not in g.keep_tables:
+            base = self.slot_base(slot)
             numels = [b.numel for b in g.blocks]
             params = [b.tensor.data_ptr() for b in g.blocks]
-            outs = [base + offsets[b.index] for b in g.blocks]
+            outs = [base + self._noise_offsets[b.index] for b in g.blocks]
             segs, items = _lib.plan_segments(numels, params, outs, self.dist, self.sms, self.max_thr)
-            g.keep_table, g.keep_nsegs, g.keep_items = _lib.to_device_table(segs, self.device), len(segs), items
+            g.keep_tables[slot] = (_lib.to_device_table(segs, self.device), len(segs), items)
             lsegs, litems = _lib.plan_linear(numels, params, outs)
-            g.kept_table, g.kept_nsegs, g.kept_items = _lib.to_device_table(lsegs, self.device), len(lsegs), litems
+            g.kept_tables[slot] = (_lib.to_device_table(lsegs, self.device), len(lsegs), litems)
+        return g.keep_tables[slot], g.kept_tables[slot]
+
+    def slot_of(self, seed: int) -> int | None:
+        """Slot holding the complete noise of `seed`, if any."""
+        for i, sd in enumerate(self.slot_seed):
+            if sd == seed:
+                return i
+        return None
+
+    def _free_slot(self) -> int:
+        """A slot for a new projection's noise: an empty one, else one whose seed left the
+        history, else the one holding the oldest history entry (that entry is then regenerated
+        until it leaves the history)."""
+        live = [item.seed for item in self.opt.history]
+        for i, sd in enumerate(self.slot_seed):
+            if sd is None:
+                return i
+        for i, sd in enumerate(self.slot_seed):
+            if sd not in live:
+                return i
+        oldest = {sd: age for age, sd in enumerate(live)}
+        return min(range(len(self.slot_seed)), key=lambda i: oldest.get(self.slot_seed[i], -1))
 
     def perturb(self, seed: int, alpha: float) -> None:
         """W <- W + alpha * Z(seed) for every selected block (muzo_optimizer.py:434-446). With the
-        noise buffer, the first pass of a seed also keeps dtype(Z) and the following passes of the
-        same seed read it back: the same values without regenerating the noise."""
+        noise pool, the first pass of a seed also keeps dtype(Z) in a slot and every later pass of
+        the same seed reads it back: the same values without regenerating the noise."""
         if not self.blocks:
             return
         stream = _lib.stream_ptr(self.device)
         alpha32 = float(np.float32(alpha))
-        if self.keep_noise and self._kept_seed == seed:
+        slot = self.slot_of(seed) if self.keep_noise else None
+        if slot is not None:
             self._mark("perturb", True)
             for g in self.perturb_groups:
-                _lib.launch("muzo_perturb_kept_noise", g.kept_table.data_ptr(), g.kept_nsegs, g.kept_items,
-                            g.dtype_code, alpha32, stream)
+                _, (table, nsegs, items) = self._slot_tables(g, slot)
+                _lib.launch("muzo_perturb_kept_noise", table.data_ptr(), nsegs, items, g.dtype_code, alpha32, stream)
             self._mark("perturb", False)
             return
         keys = self.keys_for(seed)
         dev_keys = self.uploader.upload(keys)
-        self._kept_seed = None  # the buffer is being rewritten
+        if self.keep_noise:
+            slot = self._free_slot()
+            self.slot_seed[slot] = None  # being rewritten
         self._mark("perturb", True)
         for g in self.perturb_groups:
             idx = np.fromiter((b.index for b in g.blocks), dtype=np.int64, count=len(g.blocks))
@@ -263,15 +311,16 @@ class StepEngine:
                 kptr = dev_keys.data_ptr()
             else:
                 kptr = self.uploader.upload(keys[idx]).data_ptr()
-            if self.keep_noise:
-                _lib.launch("muzo_perturb_segments_keep_noise", g.keep_table.data_ptr(), g.keep_nsegs,
-                            g.keep_items, kptr, g.dtype_code, alpha32, stream)
+            if slot is not None:
+                (table, nsegs, items), _ = self._slot_tables(g, slot)
+                _lib.launch("muzo_perturb_segments_keep_noise", table.data_ptr(), nsegs, items, kptr, g.dtype_code,
+                            alpha32, stream)
             else:
                 _lib.launch("muzo_perturb_segments", g.table.data_ptr(), g.nsegs, g.total_items, kptr,
                             g.dtype_code, self.dist, alpha32, stream)
         self._mark("perturb", False)
-        if self.keep_noise:
-            self._kept_seed = seed
+        if slot is not None:
+            self.slot_seed[slot] = seed
 
     # ------------------------------------------------------------------ step
     def _workspace_budget(self) -> int:
@@ -330,12 +379,15 @@ class StepEngine:
             rsegs, rtot = _lib.plan_segments([b.numel for b in part], [b.tensor.data_ptr() for b in part],
                                              x0_ptrs, self.dist, self.sms, self.max_thr)
             if self.keep_noise:
-                # the newest history entry can be read from the kept noise (muzo_rebuild_segments_kept)
-                base = self.noise_buffer.data_ptr()
-                rsegs["kept"] = [base + self._noise_offsets[part[int(bi)].index] for bi in rsegs["block_index"]]
+                # kept history entries are read at slot base + the block's offset in a slot
+                rsegs["kept"] = [self._noise_offsets[part[int(bi)].index] for bi in rsegs["block_index"]]
             nsegs, ntot = _lib.plan_linear([b.numel for b in part], x0_ptrs, x0_ptrs)
             ch = Chunk(part, rows, cols, code, stat_slot, _lib.to_device_table(rsegs, self.device), len(rsegs), rtot,
                        _lib.to_device_table(nsegs, self.device), ntot, pad_views=pad_views)
+            if self.keep_noise:
+                ksegs, ktot = _lib.plan_linear([b.numel for b in part], [b.tensor.data_ptr() for b in part], x0_ptrs)
+                ksegs["kept"] = [self._noise_offsets[b.index] for b in part]
+                ch.kept_rebuild_table, ch.kept_rebuild_items = _lib.to_device_table(ksegs, self.device), ktot
             ch.buf = buf
             for parity in (0, 1):
                 xs = buf.x_slot(parity)
@@ -427,13 +479,16 @@ class StepEngine:
         order = np.fromiter((b.index for ch in self.chunks for b in ch.blocks), dtype=np.int64,
                             count=self.n_slots)
         keys = np.stack([k[order] for k in seed_keys], axis=1) if horizon else np.zeros((0, 0), np.uint64)
-        payload = np.concatenate([keys.reshape(-1).view(np.uint8), alphas.view(np.uint8)])
+        # the slot of every history entry whose noise is kept (0: regenerate)
+        slots = [self.slot_of(item.seed) if self.keep_noise else None for item in hist]
+        slot_base = np.asarray([0 if sl is None else self.slot_base(sl) for sl in slots], dtype=np.uint64)
+        self.kept_entries = sum(sl is not None for sl in slots)
+        payload = np.concatenate([slot_base.view(np.uint8), keys.reshape(-1).view(np.uint8), alphas.view(np.uint8)])
         dev = self.uploader.upload(payload)
-        keys_ptr = dev.data_ptr()
+        slot_base_ptr = dev.data_ptr()
+        keys_ptr = slot_base_ptr + 8 * horizon
         alphas_ptr = keys_ptr + keys.size * 8
-
-        # the newest entry is the projection whose noise the perturbation passes kept
-        self._rebuild_kept = bool(self.keep_noise and horizon and hist[0].seed == self._kept_seed)
+        self._slot_base_ptr = slot_base_ptr
         self.state.zero_()
         base = self.state.data_ptr()
         sums_ptr, flags_ptr, stats_ptr = base, base + self.flags_off, base + self.stats_off
@@ -491,10 +546,14 @@ class StepEngine:
         s_flags = flags_ptr + 4 * ch.slot0
         self._mark("rebuild", True, stream)
         max_ctas = self.sms if self.overlap else 0
-        if self._rebuild_kept:
-            _lib.launch("muzo_rebuild_segments_kept", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs,
-                        ch.rebuild_items, keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, ch.dtype_code,
-                        normalize, inv_cs, s_sums, s_flags, max_ctas, sp)
+        if self.kept_entries and self.kept_entries == horizon:
+            _lib.launch("muzo_rebuild_kept_linear", ch.kept_rebuild_table.data_ptr(), n, ch.kept_rebuild_items,
+                        alphas_ptr, self._slot_base_ptr, horizon, ch.dtype_code, normalize, inv_cs, s_sums, s_flags,
+                        sp)
+        elif self.kept_entries:
+            _lib.launch("muzo_rebuild_segments_history", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs,
+                        ch.rebuild_items, keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, self._slot_base_ptr,
+                        horizon, ch.dtype_code, normalize, inv_cs, s_sums, s_flags, max_ctas, sp)
         else:
             _lib.launch("muzo_rebuild_segments", ch.rebuild_table.data_ptr(), ch.rebuild_nsegs, ch.rebuild_items,
                         keys_ptr + 8 * horizon * ch.slot0, alphas_ptr, horizon, self.dist, ch.dtype_code,

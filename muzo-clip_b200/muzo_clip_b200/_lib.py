@@ -78,6 +78,11 @@ _SIGNATURES = {
         [_vp, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _vp],
         _i32,
     ),
+    "muzo_rebuild_segments_history": (
+        [_vp, _i32, _i64, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _vp],
+        _i32,
+    ),
+    "muzo_rebuild_kept_linear": ([_vp, _i32, _i64, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp], _i32),
     "muzo_ns_prepare": ([_vp, _i32, _i64, _i32, _vp, _vp, _vp], _i32),
     "muzo_ns_normalize": ([_vp, _i32, _i64, _vp, _vp, _vp], _i32),
     "muzo_ns_gemm": (
@@ -117,7 +122,7 @@ class MuzoError(RuntimeError):
 KERNELS_PER_CALL = {
     "muzo_fill_noise": 1, "muzo_perturb_segments": 1, "muzo_perturb_segments_keep_noise": 1,
     "muzo_perturb_kept_noise": 1, "muzo_rebuild_segments": 1, "muzo_rebuild_segments_kept": 1,
-    "muzo_ns_prepare": 1,
+    "muzo_ns_prepare": 1, "muzo_rebuild_segments_history": 1, "muzo_rebuild_kept_linear": 1,
     "muzo_ns_normalize": 1, "muzo_ns_gemm": 1, "muzo_update_sumsq": 1, "muzo_apply_update": 1,
     "muzo_qk_scale_rows": 1, "muzo_qk_max": 3, "muzo_logits_head_max": 3, "muzo_max_merge": 1,
     "muzo_ns_normalize_noalloc": 3,

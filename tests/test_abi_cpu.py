@@ -146,6 +146,13 @@ _P = 256
     (lambda L: L.muzo_rebuild_segments_kept(_P, 1, 1024, _P, _P, 0, 1, 1, 1.0, _P, _P, 0, None), 1),
     (lambda L: L.muzo_rebuild_segments_kept(_P, 1, 1024, _P, None, 8, 1, 1, 1.0, _P, _P, 0, None), 1),
     (lambda L: L.muzo_rebuild_segments_kept(_P, 1, 1024, _P, _P, 8, 9, 1, 1.0, _P, _P, 0, None), 2),
+    (lambda L: L.muzo_rebuild_segments_history(_P, 1, 1024, _P, _P, None, 8, 1, 1, 1.0, _P, _P, 0, None), 1),
+    (lambda L: L.muzo_rebuild_segments_history(_P, 1, 1024, _P, _P, _P, 0, 1, 1, 1.0, _P, _P, 0, None), 1),
+    (lambda L: L.muzo_rebuild_segments_history(_P, 1, 1000, _P, _P, _P, 8, 1, 1, 1.0, _P, _P, 0, None), 1),
+    (lambda L: L.muzo_rebuild_segments_history(_P, 1, 1024, _P, _P, _P, 8, 7, 1, 1.0, _P, _P, 0, None), 2),
+    (lambda L: L.muzo_rebuild_kept_linear(_P, 1, 1024, _P, None, 8, 1, 1, 1.0, _P, _P, None), 1),
+    (lambda L: L.muzo_rebuild_kept_linear(_P, 1, 1024, _P, _P, 8, 1, 1, 1.0, None, _P, None), 1),
+    (lambda L: L.muzo_rebuild_kept_linear(_P, 1, 1024, _P, _P, 8, 5, 1, 1.0, _P, _P, None), 2),
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 0, 0, 1, 1, 1.0, _P, _P, 0, None), 1),  # horizon
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 1, 1, 1.0, None, _P, 0, None), 1),
     (lambda L: L.muzo_rebuild_segments(_P, 1, 1024, _P, _P, 8, 0, 9, 1, 1.0, _P, _P, 0, None), 2),

@@ -110,42 +110,53 @@ class _MixedMats(torch.nn.Module):
 
 
 @pytest.mark.parametrize("block_rows", [None, 48])
-def test_perturb_with_kept_noise_bit_exact(device, block_rows):
-    """noise_cache=True: the first pass of a seed keeps dtype(Z), later passes of that seed read
-    it back; every pass must equal the reference path's regenerated noise, and the kept noise
-    must equal the noise itself."""
+@pytest.mark.parametrize("slots", [None, 1])
+def test_perturb_with_kept_noise_bit_exact(device, monkeypatch, block_rows, slots):
+    """noise_cache=True: the first pass of a seed keeps dtype(Z) in a slot of the noise pool, later
+    passes of that seed read it back; every pass must equal the reference path's regenerated
+    noise, and the kept noise must equal the noise itself. With one slot a new seed evicts the
+    old one, which is then regenerated (and kept again) when it comes back."""
     from muzo_clip_b200 import MuZOClipOptimizer
 
+    if slots is not None:
+        monkeypatch.setenv("MUZO_NOISE_SLOTS", str(slots))
     model = _MixedMats(device)
     twin = copy.deepcopy(model)
     opt = MuZOClipOptimizer(model, distribution="normal", block_rows=block_rows, noise_cache=True)
     named = [(n, p) for n, p in twin.named_parameters() if n in set(opt.selected_parameter_names())]
     eng = opt._engine_for_step()
-    assert eng.keep_noise and eng.noise_buffer is not None and len(eng.perturb_groups) == 3
-    # keep, two reads, a new seed (rewrite), reads, an earlier seed again (rewrite)
+    assert eng.keep_noise and eng.noise_pool is not None and len(eng.perturb_groups) == 3
+    assert len(eng.slot_seed) == (slots or opt.horizon + 1)
+    # keep, two reads, a new seed, reads, the earlier seed again
     for seed, s in ((11, 1.0), (11, -2.0), (11, 1.0), (12, 1.0), (12, -2.0), (12, 1.0), (11, -1.0)):
         opt._perturb_selected(seed, s)
         tr.perturb(named, seed, s, opt.zo_eps, "normal", block_rows)
         for (n1, p1), (_, p2) in zip(model.named_parameters(), twin.named_parameters()):
             assert torch.equal(p1, p2), (n1, seed, s)
-    assert eng._kept_seed == 11
+    assert eng.slot_of(11) is not None
+    assert (eng.slot_of(12) is None) == (slots == 1)
     torch.cuda.synchronize()
     # the kept noise of every block is dtype(randn) of its key
-    off = 0
+    base = eng.slot_of(11) * eng.slot_bytes
     for b in eng.blocks:
+        off = base + eng._noise_offsets[b.index]
         nbytes = b.numel * b.tensor.element_size()
-        kept = eng.noise_buffer[off:off + nbytes].view(b.dtype).view(b.rows, b.cols)
+        kept = eng.noise_pool[off:off + nbytes].view(b.dtype).view(b.rows, b.cols)
         ref = tr.noise_like(b.tensor, 11, b.name, b.block_index, "normal")
         assert torch.equal(kept, ref), b.name
-        off += (nbytes + 255) // 256 * 256
 
 
 @pytest.mark.parametrize("block_rows", [None, 48])
-def test_steps_with_noise_cache_match_steps_without(device, block_rows):
+@pytest.mark.parametrize("slots", [None, 2])
+def test_steps_with_noise_cache_match_steps_without(device, monkeypatch, block_rows, slots):
     """Projections and steps through the public API: bit-identical weights, projections and step
-    statistics with and without the kept noise (the passes and the rebuild's newest entry read it)."""
+    statistics with and without the kept noise. With a slot for every history entry the rebuild
+    reads them all (the linear kept-noise kernel) once the history is full; with two slots it
+    reads the kept entries and regenerates the others."""
     from muzo_clip_b200 import MuZOClipOptimizer
 
+    if slots is not None:
+        monkeypatch.setenv("MUZO_NOISE_SLOTS", str(slots))
     model = _MixedMats(device)
     twin = copy.deepcopy(model)
     kw = dict(seed=9, horizon=3, min_history=1, lr=1e-3, block_rows=block_rows)
@@ -155,10 +166,11 @@ def test_steps_with_noise_cache_match_steps_without(device, block_rows):
     def loss(m):
         return float(m.a.layers[0].q_proj.weight.float().square().sum().item())
 
-    for _ in range(4):
+    for i in range(7):
         assert cached.estimate_projection(lambda: loss(model)) == plain.estimate_projection(lambda: loss(twin))
         assert cached.step() == plain.step()
-        assert cached._engine._rebuild_kept and not plain._engine._rebuild_kept
+        want = min(i + 1, 3) if slots is None else min(i + 1, 2)
+        assert cached._engine.kept_entries == want and plain._engine.kept_entries == 0
         for (n1, p1), (_, p2) in zip(model.named_parameters(), twin.named_parameters()):
             assert torch.equal(p1, p2), n1
 
@@ -171,7 +183,7 @@ def test_noise_cache_left_out_without_room(device, monkeypatch, caplog):
     opt = MuZOClipOptimizer(model, noise_cache=True)
     with caplog.at_level("WARNING"):
         eng = opt._engine_for_step()
-    assert not eng.keep_noise and eng.noise_buffer is None
+    assert not eng.keep_noise and eng.noise_pool is None
     assert any("noise_cache" in r.message for r in caplog.records)
     twin = copy.deepcopy(model)
     ref = MuZOClipOptimizer(twin)
