@@ -344,7 +344,7 @@ def run_gpu(args) -> int:
         norm_ms = max(phases.get("normalize", 0.0), 1e-9)
         norm_bytes = 4.0 * owned_elems         # bf16 momentum read and written
         h2d = 8 * len(engine.blocks) * 3 + 8 * len(engine.owned) * HORIZON + 12 * HORIZON
-        d2h = engine.state_bytes + 16
+        d2h = getattr(engine, "g_bytes", engine.state_bytes) + 16
 
         def gbs(nbytes, ms):
             return round(nbytes / (ms * 1e-3) / 1e9, 1)

@@ -341,7 +341,7 @@ class StepEngine:
         first_seen: dict[tuple[int, int, int], int] = {}
         for b in self.blocks:
             first_seen.setdefault((b.rows, b.cols, _lib.dtype_code(b.dtype)), len(first_seen))
-        desc = os.environ.get("MUZO_COLLECTIVES", "end") == "class"
+        desc = self._descending_classes()
         self.class_order = sorted(first_seen, key=lambda ck: ((-1 if desc else 1) * ck[0] * ck[1], first_seen[ck]))
         owned_by_class: dict[tuple[int, int, int], list[Block]] = {ck: [] for ck in self.class_order}
         for b in self.owned:
@@ -516,6 +516,7 @@ class StepEngine:
             ready.record(side)
             compute.wait_event(ready)
             self._finish_chunk(ch, compute, *args)
+            self._after_chunk(ch, compute)
             ev = torch.cuda.Event()
             ev.record(compute)
             done.append(ev)
@@ -535,8 +536,7 @@ class StepEngine:
             self._after_class(self.class_order[next_class])
             next_class += 1
         self._finish_collectives()
-        host = self.state.cpu().numpy()
-        return self._collect_stats(host, lr32)
+        return self._read_results(lr32)
 
     def _prepare_chunk(self, ch, stream, horizon, keys_ptr, alphas_ptr, normalize, inv_cs, sums_ptr, flags_ptr,
                        stats_ptr, status_ptr, lr32, decay, apply_decay) -> None:
@@ -594,46 +594,61 @@ class StepEngine:
         self._mark("apply", False, stream)
 
     # hooks for the sharded (multi-GPU) engine
+    def _descending_classes(self) -> bool:
+        """Shape classes largest first (per-class collectives) instead of smallest first."""
+        return os.environ.get("MUZO_COLLECTIVES", "end") == "class"
+
+    def _after_chunk(self, ch, stream) -> None:
+        """The blocks of `ch` are final once the work queued on `stream` so far has run."""
+
     def _after_class(self, class_key) -> None:
         pass
 
     def _finish_collectives(self) -> None:
         pass
 
-    def _collect_stats(self, host: np.ndarray, lr32: float) -> dict[int, dict[str, float]]:
+    def _read_results(self, lr32: float) -> dict[int, dict[str, float]]:
+        """The step's per-block results in one device-to-host copy (owned blocks only)."""
+        host = self.state.cpu().numpy()
         n = max(self.n_slots, 1)
         sums = host[: self.sums_bytes].view(np.float64).reshape(n, _lib.NSUMS)
         flags = host[self.flags_off: self.flags_off + 4 * (n + 4)].view(np.int32)
         stats = host[self.stats_off: self.stats_off + 4 * _lib.NSTATS * n].view(np.float32).reshape(n, _lib.NSTATS)
-        status = int(flags[n])
+        pairs, slot = [], 0
+        for ch in self.chunks:
+            for b in ch.blocks:
+                pairs.append((b, slot))
+                slot += 1
+        return self._stats_from(sums, flags, stats, int(flags[n]), pairs, lr32)
+
+    def _stats_from(self, sums, flags, stats, status: int, pairs, lr32: float) -> dict[int, dict[str, float]]:
+        """Per-block statistics (muzo_optimizer.py:342-357) from the step's sums, flags and
+        statistics; `pairs` lists (block, row of that block in the arrays)."""
         if status != 0:
             raise _lib.MuzoError(f"Newton-Schulz GEMM reported status {status} (a bounded wait expired); the "
                                  "weights this step updated are unspecified: restore them from a checkpoint")
         out: dict[int, dict[str, float]] = {}
         lr = np.float32(lr32)
-        slot = 0
-        for ch in self.chunks:
-            for b in ch.blocks:
-                s = sums[slot]
-                st = stats[slot]
-                numel = float(b.numel)
-                zeroed = bool(st[_lib.STAT_ZEROED] != 0)
-                rms_w = np.float32(math.sqrt(s[_lib.SUM_W2] / numel))
-                denom = np.float32(rms_w + np.float32(1e-12))
-                if zeroed:
-                    update_rms, ratio = 0.0, 0.0
-                else:
-                    rms_u = np.float32(math.sqrt(s[_lib.SUM_U2_CLIPPED] / numel))
-                    update_rms_f = np.float32(rms_u * lr)
-                    update_rms = float(update_rms_f)
-                    ratio = float(np.float32(update_rms_f / denom))
-                out[b.index] = {
-                    "update_rms": update_rms,
-                    "ratio": ratio,
-                    "ratio_before": float(st[_lib.STAT_RATIO_BEFORE]),
-                    "clip": float(st[_lib.STAT_CLIP_FACTOR]),
-                    "zeroed": zeroed,
-                    "flags": int(flags[slot]),
-                }
-                slot += 1
+        for b, slot in pairs:
+            s = sums[slot]
+            st = stats[slot]
+            numel = float(b.numel)
+            zeroed = bool(st[_lib.STAT_ZEROED] != 0)
+            rms_w = np.float32(math.sqrt(s[_lib.SUM_W2] / numel))
+            denom = np.float32(rms_w + np.float32(1e-12))
+            if zeroed:
+                update_rms, ratio = 0.0, 0.0
+            else:
+                rms_u = np.float32(math.sqrt(s[_lib.SUM_U2_CLIPPED] / numel))
+                update_rms_f = np.float32(rms_u * lr)
+                update_rms = float(update_rms_f)
+                ratio = float(np.float32(update_rms_f / denom))
+            out[b.index] = {
+                "update_rms": update_rms,
+                "ratio": ratio,
+                "ratio_before": float(st[_lib.STAT_RATIO_BEFORE]),
+                "clip": float(st[_lib.STAT_CLIP_FACTOR]),
+                "zeroed": zeroed,
+                "flags": int(flags[slot]),
+            }
         return out

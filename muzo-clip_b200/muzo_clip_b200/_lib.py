@@ -30,6 +30,7 @@ F32, BF16, F16 = 0, 1, 2
 NORMAL, RADEMACHER = 0, 1
 EPI_STORE, EPI_POLY, EPI_UPDATE = 0, 1, 2
 ITEMS_PER_CTA = 1024
+IPC_HANDLE_BYTES = 64
 NSUMS = 8
 SUM_M2, SUM_X2, SUM_W2, SUM_U2, SUM_U2_CLIPPED = 0, 1, 2, 3, 4
 FLAG_NONFINITE_INPUT, FLAG_ZERO_NORM, FLAG_NONFINITE_OUTPUT = 1, 2, 4
@@ -104,6 +105,10 @@ _SIGNATURES = {
     "muzo_logits_head_max": ([_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp], _i32),
     "muzo_max_merge": ([_vp, _vp, _vp, _i64, _vp], _i32),
     "muzo_ns_normalize_noalloc": ([_vp, _vp, _vp, _i32, _i32, _vp, _vp], _i32),
+    "muzo_ipc_export": ([_vp, _vp, _vp, _vp], _i32),
+    "muzo_ipc_import": ([_vp, _vp], _i32),
+    "muzo_ipc_close": ([_vp], _i32),
+    "muzo_push_blocks": ([_vp, _vp, _vp, _i32, _vp], _i32),
 }
 
 for _name, (_args, _ret) in _SIGNATURES.items():
@@ -125,7 +130,8 @@ KERNELS_PER_CALL = {
     "muzo_ns_prepare": 1, "muzo_rebuild_segments_history": 1, "muzo_rebuild_kept_linear": 1,
     "muzo_ns_normalize": 1, "muzo_ns_gemm": 1, "muzo_update_sumsq": 1, "muzo_apply_update": 1,
     "muzo_qk_scale_rows": 1, "muzo_qk_max": 3, "muzo_logits_head_max": 3, "muzo_max_merge": 1,
-    "muzo_ns_normalize_noalloc": 3,
+    "muzo_ns_normalize_noalloc": 3, "muzo_ipc_export": 0, "muzo_ipc_import": 0, "muzo_ipc_close": 0,
+    "muzo_push_blocks": 0,
 }
 launch_count = 0
 

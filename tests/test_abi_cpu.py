@@ -176,6 +176,14 @@ _P = 256
     (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 2, 1.0, 0.0, 8, 8, 8, 1, 1, None, None, None, None, None), 1),
     (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 16, 1, 0, None, None, None, None, None), 1),
     (lambda L: L.muzo_ns_gemm(_P + 8, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, None, 0, 0.0, 0.0, 8, 8, 8, 1, 0, None, None, None, None, None), 3),
+    # weight exchange: null arguments and negative counts are rejected before any CUDA call
+    (lambda L: L.muzo_ipc_export(None, _P, _P, None), 1),
+    (lambda L: L.muzo_ipc_export(_P, None, _P, None), 1),
+    (lambda L: L.muzo_ipc_import(None, _P), 1),
+    (lambda L: L.muzo_ipc_close(None), 1),
+    (lambda L: L.muzo_push_blocks(None, None, None, -1, None), 1),
+    (lambda L: L.muzo_push_blocks(None, _P, _P, 2, None), 1),
+    (lambda L: L.muzo_push_blocks(None, None, None, 0, None), 0),
     # sums of squares only with the update epilogue, and then with scales and flags
     (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 1, 1.0, 1.0, 8, 8, 8, 1, 0, _P, _P, _P, None, None), 1),
     (lambda L: L.muzo_ns_gemm(_P, 8, 0, 0, _P, 8, 0, 0, _P, 8, 0, _P, 2, 1.0, 0.0, 8, 8, 8, 1, 0, _P, None, _P, None, None), 1),

@@ -1,9 +1,10 @@
 """Host logic of the sharded step on two gloo ranks (CPU, no GPU).
 
 Covers: the LPT ownership is identical on every rank; owners' updated blocks reach every rank
-through the class-by-class broadcasts; per-block statistics combine to the same StepStats on all
-ranks; the SPSA losses are averaged over the group so every rank derives the same projection;
-QK-Clip maxima captured on per-rank batches are max-reduced so every rank clips alike.
+through the broadcasts of the collective exchange; per-block statistics scattered into global
+buffers and summed over the group give every rank every block's statistics; the peer exchange's
+address table; the SPSA losses are averaged over the group so every rank derives the same
+projection; QK-Clip maxima captured on per-rank batches are max-reduced so every rank clips alike.
 """
 
 from __future__ import annotations
@@ -23,6 +24,7 @@ ROOT = Path(__file__).resolve().parent.parent
 class _Block:
     def __init__(self, index, rows, cols, tensor):
         self.index, self.rows, self.cols, self.tensor, self.dtype = index, rows, cols, tensor, tensor.dtype
+        self.numel = rows * cols
 
 
 def _worker(rank: int, world: int, store: str, out_dir: str) -> None:
@@ -30,28 +32,62 @@ def _worker(rank: int, world: int, store: str, out_dir: str) -> None:
     # file rendezvous: no TCP port to race for on a shared host
     dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=world)
     try:
-        from muzo_clip_b200._engine import ns_flops, partition_blocks
+        import numpy as np
+
+        from muzo_clip_b200 import _lib
+        from muzo_clip_b200._engine import StepEngine, ns_flops, partition_blocks
         from muzo_clip_b200.distributed import ShardedStepEngine
 
         shapes = [(64, 32), (16, 32), (16, 32), (64, 32), (96, 32), (96, 32), (32, 96)] * 3
         blocks = [_Block(i, r, c, torch.full((r, c), -1.0)) for i, (r, c) in enumerate(shapes)]
         owner = partition_blocks([ns_flops(r, c, 5) for r, c in shapes], world)
 
-        class Fake:  # the collective parts of ShardedStepEngine on CPU tensors
+        class Fake:  # the host and collective parts of ShardedStepEngine on CPU tensors
             _after_class = ShardedStepEngine._after_class
             _finish_collectives = ShardedStepEngine._finish_collectives
             _class_blocks = ShardedStepEngine._class_blocks
             _broadcast = ShardedStepEngine._broadcast
+            scatter_owned_results = ShardedStepEngine.scatter_owned_results
+            reduce_results = ShardedStepEngine.reduce_results
+            _read_results = ShardedStepEngine._read_results
+            _stats_from = StepEngine._stats_from
             gather_stats = ShardedStepEngine.gather_stats
             _code = staticmethod(ShardedStepEngine._code)
 
         eng = Fake()
         eng.blocks, eng.owner, eng.world, eng.group = blocks, owner, world, dist.group.WORLD
         eng._pending, eng._handles, eng._global_ranks, eng.device = [], [], list(range(world)), torch.device("cpu")
+        eng.exchange, eng._peer = "nccl", None
+        owned = [b for b in blocks if owner[b.index] == rank]
+        # the step's per-block state of this rank's blocks, in slot order, as _build_step lays it out
+        n_owned, n = len(owned), len(blocks)
+        eng.n_slots = n_owned
+        eng.sums_bytes = 8 * _lib.NSUMS * max(n_owned, 1)
+        eng.flags_off = eng.sums_bytes
+        eng.stats_off = (eng.flags_off + 4 * (max(n_owned, 1) + 4) + 15) // 16 * 16
+        eng.state_bytes = eng.stats_off + 4 * _lib.NSTATS * max(n_owned, 1)
+        eng.state = torch.zeros(eng.state_bytes, dtype=torch.uint8)
+        sums = eng.state[:eng.sums_bytes].view(torch.float64).view(-1, _lib.NSUMS)
+        flags = eng.state[eng.flags_off:eng.flags_off + 4 * (max(n_owned, 1) + 4)].view(torch.int32)
+        stats = eng.state[eng.stats_off:eng.state_bytes].view(torch.float32).view(-1, _lib.NSTATS)
+        for slot, b in enumerate(owned):
+            numel = b.rows * b.cols
+            sums[slot, _lib.SUM_W2] = numel * 0.02 ** 2          # rms(W) = 0.02
+            sums[slot, _lib.SUM_U2_CLIPPED] = numel * (1.0 + b.index) ** 2   # rms(U) = 1 + index
+            stats[slot, _lib.STAT_CLIP_FACTOR] = 0.5
+            flags[slot] = b.index % 2
+        eng.g_sums_bytes = 8 * _lib.NSUMS * n
+        eng.g_flags_off = eng.g_sums_bytes
+        eng.g_stats_off = (eng.g_flags_off + 4 * (n + 4) + 15) // 16 * 16
+        eng.g_bytes = eng.g_stats_off + 4 * _lib.NSTATS * n
+        eng.g_state = torch.zeros(eng.g_bytes, dtype=torch.uint8)
+        eng.g_sums = eng.g_state[:eng.g_sums_bytes].view(torch.float64).view(n, _lib.NSUMS)
+        eng.g_flags = eng.g_state[eng.g_flags_off:eng.g_flags_off + 4 * (n + 4)].view(torch.int32)
+        eng.g_stats = eng.g_state[eng.g_stats_off:eng.g_bytes].view(torch.float32).view(n, _lib.NSTATS)
+        eng.owned_global = torch.tensor([b.index for b in owned], dtype=torch.int64)
         # owners "update" their blocks; everyone else holds stale values
-        for b in blocks:
-            if owner[b.index] == rank:
-                b.tensor.fill_(float(b.index))
+        for b in owned:
+            b.tensor.fill_(float(b.index))
         class_order = []
         for b in blocks:
             ck = (b.rows, b.cols, eng._code(b))
@@ -61,10 +97,12 @@ def _worker(rank: int, world: int, store: str, out_dir: str) -> None:
             eng._after_class(ck)
         eng._finish_collectives()
         ok = all(bool((b.tensor == float(b.index)).all()) for b in blocks)
-        stats = eng.gather_stats({b.index: {"update_rms": 0.1 * b.index, "ratio": 0.01 * b.index}
-                                  for b in blocks if owner[b.index] == rank})
-        stats_ok = sorted(stats) == list(range(len(blocks))) and all(
-            abs(stats[i]["update_rms"] - 0.1 * i) < 1e-12 for i in stats)
+        lr = 1e-3
+        per_block = eng.gather_stats(eng._read_results(lr))
+        want_rms = {b.index: float(np.float32(np.float32(1.0 + b.index) * np.float32(lr))) for b in blocks}
+        stats_ok = sorted(per_block) == list(range(n)) and all(
+            abs(per_block[i]["update_rms"] - want_rms[i]) <= 1e-6 * want_rms[i] and per_block[i]["clip"] == 0.5
+            and per_block[i]["flags"] == i % 2 for i in per_block)
 
         # loss averaging of estimate_projection over the group
         import muzo_clip_b200.muzo_optimizer as mo
@@ -96,6 +134,8 @@ def _worker(rank: int, world: int, store: str, out_dir: str) -> None:
 
 
 def test_sharded_collectives_on_two_gloo_ranks(tmp_path):
+    """NCCL-style exchange (broadcasts) and the global per-block statistics, summed over the
+    group: every rank ends with every block's final value and every block's statistics."""
     world = 2
     mp.start_processes(_worker, args=(world, str(tmp_path / "store"), str(tmp_path)), nprocs=world,
                        start_method="spawn")
@@ -103,6 +143,30 @@ def test_sharded_collectives_on_two_gloo_ranks(tmp_path):
     for ok, stats_ok, same_p, owner in lines:
         assert ok == "1" and stats_ok == "1" and same_p == "1"
     assert lines[0][3] == lines[1][3]  # identical ownership on both ranks
+
+
+def test_peer_destinations_open_each_handle_once():
+    """The peer exchange's address table from the handles every rank exported: one mapping per
+    distinct (rank, allocation), every owned block's address in every peer = base + offset."""
+    sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
+    from muzo_clip_b200.distributed import peer_destinations
+
+    world, nblocks = 3, 5
+    # rank r's blocks 0-2 share one allocation, blocks 3-4 another
+    gathered = [[(b"h%d-%d" % (r, 0 if i < 3 else 1), 4096 * i) for i in range(nblocks)] for r in range(world)]
+    opened = []
+
+    def opener(handle):
+        opened.append(handle)
+        return 1 << 40 | (len(opened) << 32)
+
+    dst, bases = peer_destinations(gathered, [0, 3, 4], 1, opener)
+    assert sorted(dst) == [0, 2] and len(opened) == len(set(opened)) == 4
+    for r in (0, 2):
+        assert sorted(dst[r]) == [0, 3, 4]
+        for i in (0, 3, 4):
+            handle, off = gathered[r][i]
+            assert dst[r][i] == bases[(r, handle)] + off
 
 
 def _qk_worker(rank: int, world: int, store: str, out_dir: str) -> None:

@@ -1,7 +1,8 @@
 """The sharded step on 2 GPUs (NCCL, one process per GPU) against one GPU.
 
 Every rank perturbs its own replica; each block is rebuilt, orthogonalised and applied by its
-owner only and broadcast to the others. With the same seeds and losses the weights must come out
+owner only and placed in the other rank's replica (copy-engine pushes through peer mappings, or
+NCCL broadcasts). With the same seeds and losses the weights must come out
 bit-identical on both ranks and equal to the single-GPU run: the kernels work per matrix, so the
 partition and the batch composition change nothing. With per-rank batches (each rank's closure
 returns its own loss) the ranks average the two SPSA losses, so they must match one GPU whose
@@ -43,12 +44,13 @@ def _build(device):
 RANK_SHIFT = (1.0, -1.0)
 
 
-def _run(model, process_group=None, shift=None) -> dict[str, torch.Tensor]:
+def _run(model, process_group=None, shift=None, noise_cache=False) -> dict[str, torch.Tensor]:
     """``shift``: None (same batch everywhere), a rank's own offset, or "mean" (one GPU playing
     both ranks)."""
     from muzo_clip_b200 import MuZOClipOptimizer
 
-    opt = MuZOClipOptimizer(model, seed=21, horizon=4, min_history=2, process_group=process_group)
+    opt = MuZOClipOptimizer(model, seed=21, horizon=4, min_history=2, process_group=process_group,
+                            noise_cache=noise_cache)
     w0 = model.layers[0].up_proj.weight
 
     def closure():
@@ -63,12 +65,20 @@ def _run(model, process_group=None, shift=None) -> dict[str, torch.Tensor]:
         opt.estimate_projection(closure)
         opt.step()
     torch.cuda.synchronize()
-    return {n: p.detach().cpu() for n, p in model.named_parameters()}
+    out = {n: p.detach().cpu() for n, p in model.named_parameters()}
+    if hasattr(opt._engine, "close"):
+        if process_group is not None:
+            import torch.distributed as dist
+
+            dist.barrier(group=process_group)   # no peer still pushes into this rank
+        opt._engine.close()
+    return out
 
 
-def _worker(rank: int, world: int, store: str, out_prefix: str, own_batches: bool = False) -> None:
+def _worker(rank: int, world: int, store: str, out_prefix: str, own_batches: bool = False, exchange: str = "peer",
+            noise_cache: bool = False) -> None:
     sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
-    os.environ.update(NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0", MUZO_EXCHANGE=exchange)
     import torch.distributed as dist
 
     torch.cuda.set_device(rank)
@@ -77,21 +87,25 @@ def _worker(rank: int, world: int, store: str, out_prefix: str, own_batches: boo
                             timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
     try:
         weights = _run(_build(torch.device("cuda", rank)), dist.group.WORLD,
-                       RANK_SHIFT[rank] if own_batches else None)
+                       RANK_SHIFT[rank] if own_batches else None, noise_cache)
         torch.save(weights, f"{out_prefix}.{rank}")
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("own_batches", [False, True], ids=["same_batch", "per_rank_batches"])
-def test_two_ranks_match_one_gpu(tmp_path, own_batches):
+@pytest.mark.parametrize("own_batches,exchange,noise_cache", [(False, "peer", False), (True, "peer", False),
+                                                             (False, "nccl", False), (True, "peer", True)],
+                         ids=["same_batch-peer", "per_rank_batches-peer", "same_batch-nccl", "per_rank-peer-kept"])
+def test_two_ranks_match_one_gpu(tmp_path, own_batches, exchange, noise_cache):
+    """Peer exchange (owners push their blocks into the other rank's parameters with copy-engine
+    copies) and NCCL broadcasts; with and without the kept-noise pool."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
 
     ref = _run(_build(torch.device("cuda", 0)), shift="mean" if own_batches else None)
-    mp.start_processes(_worker, args=(2, str(tmp_path / "store"), str(tmp_path / "w"), own_batches), nprocs=2,
-                       start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(2, str(tmp_path / "store"), str(tmp_path / "w"), own_batches, exchange,
+                                      noise_cache), nprocs=2, start_method="spawn", join=True)
     moved = sum(int(not torch.equal(ref[n], v)) for n, v in _build(torch.device("cpu")).named_parameters())
     assert moved == len(SHAPES)  # every selected matrix was updated
     for r in range(2):
