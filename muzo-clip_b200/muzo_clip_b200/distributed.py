@@ -134,16 +134,7 @@ class ShardedStepEngine(StepEngine):
 
     def _build_step(self) -> None:
         super()._build_step()
-        n = len(self.blocks)
-        # global per-block buffers: sums (f64) | flags + 4 status words (i32) | statistics (f32)
-        self.g_sums_bytes = 8 * _lib.NSUMS * n
-        self.g_flags_off = self.g_sums_bytes
-        self.g_stats_off = (self.g_flags_off + 4 * (n + 4) + 15) // 16 * 16
-        self.g_bytes = self.g_stats_off + 4 * _lib.NSTATS * n
-        self.g_state = torch.zeros(self.g_bytes, dtype=torch.uint8, device=self.device)
-        self.g_sums = self.g_state[:self.g_sums_bytes].view(torch.float64).view(n, _lib.NSUMS)
-        self.g_flags = self.g_state[self.g_flags_off:self.g_flags_off + 4 * (n + 4)].view(torch.int32)
-        self.g_stats = self.g_state[self.g_stats_off:self.g_bytes].view(torch.float32).view(n, _lib.NSTATS)
+        self._alloc_global_results(len(self.blocks))
         order = [b.index for ch in self.chunks for b in ch.blocks]
         self.owned_global = torch.tensor(order, dtype=torch.int64, device=self.device)
         self.comm_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
@@ -157,6 +148,19 @@ class ShardedStepEngine(StepEngine):
                 logger.warning("parameter memory cannot be shared between the ranks' processes; the updated "
                                "weights are exchanged by NCCL broadcasts")
                 self.exchange = "nccl"
+
+    def _alloc_global_results(self, n: int) -> None:
+        """One float64 buffer of per-block results indexed by global block: sums [n, NSUMS],
+        flags and the 4 status words [n + 4], statistics [n, NSTATS] (integers and fp32 values are
+        exact in fp64, and each block's entries are nonzero on its owner only, so a sum over the
+        group gathers them)."""
+        a = n * _lib.NSUMS
+        b = a + n + 4
+        self.g_state = torch.zeros(b + n * _lib.NSTATS, dtype=torch.float64, device=self.device)
+        self.g_sums = self.g_state[:a].view(n, _lib.NSUMS)
+        self.g_flags = self.g_state[a:b]
+        self.g_stats = self.g_state[b:].view(n, _lib.NSTATS)
+        self.g_bytes = 8 * self.g_state.numel()
 
     # ------------------------------------------------------------------ exchange hooks
     def _after_chunk(self, ch, stream) -> None:
@@ -225,30 +229,22 @@ class ShardedStepEngine(StepEngine):
             flags = self.state[self.flags_off:self.flags_off + 4 * (max(n_owned, 1) + 4)].view(torch.int32)
             stats = self.state[self.stats_off:self.state_bytes].view(torch.float32).view(-1, _lib.NSTATS)[:n_owned]
             self.g_sums.index_copy_(0, self.owned_global, sums)
-            self.g_flags[:n].index_copy_(0, self.owned_global, flags[:n_owned])
-            self.g_stats.index_copy_(0, self.owned_global, stats)
-            self.g_flags[n:n + 4].copy_(flags[n_owned:n_owned + 4])
+            self.g_flags[:n].index_copy_(0, self.owned_global, flags[:n_owned].to(torch.float64))
+            self.g_stats.index_copy_(0, self.owned_global, stats.to(torch.float64))
+            self.g_flags[n:n + 4].copy_(flags[n_owned:n_owned + 4].to(torch.float64))
 
     def reduce_results(self) -> None:
-        """Sum the global per-block buffers over the group (one coalesced group of all-reduces)."""
-        if self.world <= 1:
-            return
-        tensors = (self.g_sums, self.g_flags, self.g_stats)
-        manager = getattr(dist, "_coalescing_manager", None)
-        if dist.get_backend(self.group) == "nccl" and manager is not None:
-            with manager(group=self.group, device=self.device):
-                for t in tensors:
-                    dist.all_reduce(t, group=self.group)
-        else:
-            for t in tensors:
-                dist.all_reduce(t, group=self.group)
+        """Sum the global per-block buffer over the group (one all-reduce)."""
+        if self.world > 1:
+            dist.all_reduce(self.g_state, group=self.group)
 
     def _read_results(self, lr32: float) -> dict[int, dict[str, float]]:
         host = self.g_state.cpu().numpy()
         n = len(self.blocks)
-        sums = host[:self.g_sums_bytes].view(np.float64).reshape(n, _lib.NSUMS)
-        flags = host[self.g_flags_off:self.g_flags_off + 4 * (n + 4)].view(np.int32)
-        stats = host[self.g_stats_off:self.g_bytes].view(np.float32).reshape(n, _lib.NSTATS)
+        a, b = n * _lib.NSUMS, n * _lib.NSUMS + n + 4
+        sums = host[:a].reshape(n, _lib.NSUMS)
+        flags = host[a:b].astype(np.int64)
+        stats = host[b:].astype(np.float32).reshape(n, _lib.NSTATS)
         return self._stats_from(sums, flags[:n], stats, int(flags[n]), [(b, b.index) for b in self.blocks], lr32)
 
     def gather_stats(self, per_block: dict[int, dict]) -> dict[int, dict]:

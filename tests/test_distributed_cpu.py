@@ -76,14 +76,7 @@ def _worker(rank: int, world: int, store: str, out_dir: str) -> None:
             sums[slot, _lib.SUM_U2_CLIPPED] = numel * (1.0 + b.index) ** 2   # rms(U) = 1 + index
             stats[slot, _lib.STAT_CLIP_FACTOR] = 0.5
             flags[slot] = b.index % 2
-        eng.g_sums_bytes = 8 * _lib.NSUMS * n
-        eng.g_flags_off = eng.g_sums_bytes
-        eng.g_stats_off = (eng.g_flags_off + 4 * (n + 4) + 15) // 16 * 16
-        eng.g_bytes = eng.g_stats_off + 4 * _lib.NSTATS * n
-        eng.g_state = torch.zeros(eng.g_bytes, dtype=torch.uint8)
-        eng.g_sums = eng.g_state[:eng.g_sums_bytes].view(torch.float64).view(n, _lib.NSUMS)
-        eng.g_flags = eng.g_state[eng.g_flags_off:eng.g_flags_off + 4 * (n + 4)].view(torch.int32)
-        eng.g_stats = eng.g_state[eng.g_stats_off:eng.g_bytes].view(torch.float32).view(n, _lib.NSTATS)
+        ShardedStepEngine._alloc_global_results(eng, n)
         eng.owned_global = torch.tensor([b.index for b in owned], dtype=torch.int64)
         # owners "update" their blocks; everyone else holds stale values
         for b in owned:
