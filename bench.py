@@ -566,7 +566,7 @@ def _run_one_case(args) -> int:
         fl = args.batch * ns_flops(args.rows, args.cols, 5)
         out.update(rows=args.rows, cols=args.cols, batch=args.batch, symmetric=not args.dense, ms=round(ms, 3),
                    dense_tflops=round(fl / ms / 1e9, 1), status=int(status[0]))
-    elif args.case in ("perturb", "rebuild"):
+    elif args.case in ("perturb", "rebuild", "apply", "normalize"):
         numel = args.numel
         cols = 4096 if numel % 4096 == 0 else 1
         w = torch.empty((numel // cols, cols), dtype=torch.bfloat16, device=device)
@@ -593,7 +593,24 @@ def _run_one_case(args) -> int:
             run = lambda: _lib.launch("muzo_perturb_segments", table.data_ptr(), len(segs), total,  # noqa: E731
                                       keys.data_ptr(), _lib.BF16, dist_code, 1e-3, sp)
             nbytes = 4.0 * numel
-        else:
+        elif args.case == "rebuild" and args.keep:
+            # every history entry read from a kept-noise slot: H bf16 reads + W read + bf16(M)
+            # write = 2H + 4 B per element
+            x = torch.empty_like(w)
+            pool = torch.empty((args.horizon, numel), dtype=torch.bfloat16, device=device)
+            pool.normal_()
+            lsegs, ltotal = _lib.plan_linear([numel], [w.data_ptr()], [x.data_ptr()])
+            lsegs["kept"] = [0]
+            table = _lib.to_device_table(lsegs, device)
+            bases = torch.tensor([pool[h].data_ptr() for h in range(args.horizon)], dtype=torch.int64, device=device)
+            alphas = torch.full((args.horizon,), 0.1, dtype=torch.float32, device=device)
+            sums = torch.zeros(_lib.NSUMS, dtype=torch.float64, device=device)
+            flags = torch.zeros(4, dtype=torch.int32, device=device)
+            run = lambda: _lib.launch("muzo_rebuild_kept_linear", table.data_ptr(), len(lsegs), ltotal,  # noqa: E731
+                                      alphas.data_ptr(), bases.data_ptr(), args.horizon, _lib.BF16, 1, 0.5,
+                                      sums.data_ptr(), flags.data_ptr(), sp)
+            nbytes = (2.0 * args.horizon + 4.0) * numel
+        elif args.case == "rebuild":
             x = torch.empty_like(w)
             segs, total = _lib.plan_segments([numel], [w.data_ptr()], [x.data_ptr()], dist_code, sms, thr)
             table = _lib.to_device_table(segs, device)
@@ -604,6 +621,30 @@ def _run_one_case(args) -> int:
                                       keys.data_ptr(), alphas.data_ptr(), args.horizon, dist_code, _lib.BF16, 1, 0.5,
                                       sums.data_ptr(), flags.data_ptr(), 0, sp)
             nbytes = 4.0 * numel  # bf16(M) write + W read
+        else:
+            # the update apply (X read, W read + written: 6 B per element) or the normalisation of
+            # the rebuilt momentum (X read + written: 4 B per element), on one block
+            x = torch.empty_like(w)
+            x.normal_(0.0, 1.0 / math.sqrt(numel))
+            segs, total = _lib.plan_linear([numel], [w.data_ptr()], [x.data_ptr()])
+            table = _lib.to_device_table(segs, device)
+            sums = torch.zeros(_lib.NSUMS, dtype=torch.float64, device=device)
+            sums[_lib.SUM_X2] = 1.0
+            sums[_lib.SUM_M2] = 1.0
+            sums[_lib.SUM_W2] = numel * 0.02 ** 2
+            sums[_lib.SUM_U2] = float(numel)
+            flags = torch.zeros(4, dtype=torch.int32, device=device)
+            stats = torch.zeros(_lib.NSTATS, dtype=torch.float32, device=device)
+            scales = torch.ones(1, dtype=torch.float32, device=device)
+            if args.case == "apply":
+                run = lambda: _lib.launch("muzo_apply_update", table.data_ptr(), len(segs), total,  # noqa: E731
+                                          _lib.BF16, scales.data_ptr(), 1e-5, 0.01, 1, 1.0 - 1e-7, sums.data_ptr(),
+                                          flags.data_ptr(), stats.data_ptr(), sp)
+                nbytes = 6.0 * numel
+            else:
+                run = lambda: _lib.launch("muzo_ns_normalize", table.data_ptr(), len(segs), total,  # noqa: E731
+                                          sums.data_ptr(), flags.data_ptr(), sp)
+                nbytes = 4.0 * numel
         for _ in range(args.warmup):
             run()
         # working sets below 1 GiB (8 x the 126 MB L2) could be partly served from L2 on repeated
@@ -612,7 +653,7 @@ def _run_one_case(args) -> int:
             else None
         ms = _event_ms(run, args.steps, stream, flush)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        out.update(numel=numel, dist="kept" if args.keep and args.case == "perturb" else args.dist,
+        out.update(numel=numel, dist="kept" if args.keep and args.case in ("perturb", "rebuild") else args.dist,
                    horizon=args.horizon if args.case == "rebuild" else None,
                    ms=round(ms, 4), gbs=round(gbs, 1), hbm_frac=round(gbs / peaks["hbm_gbs"], 4),
                    l2="flushed between passes" if flush is not None else "working set larger than L2")
@@ -639,7 +680,7 @@ def _run_one_case(args) -> int:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", default=None, choices=["ns", "perturb", "rebuild", "qk"],
+    ap.add_argument("--case", default=None, choices=["ns", "perturb", "rebuild", "apply", "normalize", "qk"],
                     help="run one kernel family on a small workload instead of the optimizer step")
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)
@@ -659,7 +700,8 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--keep", action="store_true",
-                    help="perturb case: time a pass that reads kept noise (muzo_perturb_kept_noise)")
+                    help="perturb case: a pass that reads kept noise (muzo_perturb_kept_noise); rebuild case: "
+                         "every history entry read from kept noise (muzo_rebuild_kept_linear)")
     ap.add_argument("--no-noise-cache", action="store_true",
                     help="time only the default configuration (every pass and history entry regenerates its noise)")
     ap.add_argument("--no-variant", action="store_true",

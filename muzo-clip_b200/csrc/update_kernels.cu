@@ -50,6 +50,17 @@ __device__ __forceinline__ double block_sum(double v) {
 }
 
 // ------------------------------------------------------------------ normalisation
+// bf16(x / d) for the IEEE round-to-nearest quotient, through the product with the correctly
+// rounded reciprocal r = 1/d: |x * r - x / d| stays within 2 fp32 ulps of the quotient, so both
+// round to the same bf16 value unless the product lies within 4 ulps of a bf16 rounding midpoint
+// (low 16 bits of the fp32 pattern near 0x8000) or is not finite; those few take the division.
+__device__ __forceinline__ float bf16_quotient(float x, float d, float r) {
+  const float q = x * r;
+  const uint32_t low = __float_as_uint(q) & 0xffffu;
+  if (low - 0x7ffcu <= 8u || !isfinite(q)) return __fdiv_rn(x, d);
+  return q;
+}
+
 // X <- bf16(X / (||X||_F + 1e-7)) (newton_schulz.py:46-53): the norm is the fp32 Frobenius norm
 // of the bf16 values, 1e-7 is added in fp32 and the division is IEEE round-to-nearest.
 __global__ void __launch_bounds__(kElemThreads)
@@ -60,6 +71,7 @@ ns_normalize_kernel(const muzo_segment* __restrict__ segs, int nsegs, const doub
   const double m2 = bs[MUZO_SUM_M2];
   const float nrm = static_cast<float>(sqrt(bs[MUZO_SUM_X2]));
   const float denom = __fadd_rn(nrm, 1e-7f);
+  const float recip = __frcp_rn(denom);
   // zeropower_via_newtonschulz5 returns zeros for a zero or non-finite fp32 norm (35-43)
   if (v.local_item0 == 0 && threadIdx.x == 0 && (!(m2 > 0.0) || !isfinite(m2)))
     atomicOr(flags + v.block, MUZO_FLAG_ZERO_NORM);
@@ -73,7 +85,7 @@ ns_normalize_kernel(const muzo_segment* __restrict__ segs, int nsegs, const doub
       float x[8];
       load8(v.out, li, MUZO_BF16, x);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = __fdiv_rn(x[k], denom);
+      for (int k = 0; k < 8; ++k) x[k] = bf16_quotient(x[k], denom, recip);
       store8(v.out, li, MUZO_BF16, x);
     } else {
 #pragma unroll
@@ -222,6 +234,34 @@ __device__ __forceinline__ ApplyScalars block_scalars(const double* bs, int32_t 
   return s;
 }
 
+// One element of the apply: U = x * scale (times the clip factor), W = dtype(W - lr * dtype(U)),
+// then the decay multiply, each rounding as the reference's tensor ops.
+template <int DTYPE>
+__device__ __forceinline__ void apply8(float (&x)[8], float (&w)[8], const ApplyScalars& sc, float scale, float neg_lr,
+                                       int apply_decay, float decay) {
+  float u[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    u[k] = sc.zeroed ? 0.0f : x[k] * scale;           // U.mul_(sqrt(max)*muon_scale)
+    if (sc.clipped) u[k] = u[k] * sc.clip;             // U.mul_(clip / ratio)
+  }
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) round2_to(u[k], u[k + 1], DTYPE);       // U.to(block.dtype)
+#pragma unroll
+  for (int k = 0; k < 8; ++k) w[k] = __fmaf_rn(neg_lr, u[k], w[k]);      // block.add_(U, alpha=-lr)
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) round2_to(w[k], w[k + 1], DTYPE);
+  if (apply_decay) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = w[k] * decay;                     // block.mul_(1 - lr*wd)
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) round2_to(w[k], w[k + 1], DTYPE);
+  }
+}
+
+// Apply of every block (muzo_optimizer.py:340-353). The sum of the clipped update's squares
+// (the reported update_rms) is clip^2 times the sum of U^2 the last Newton-Schulz GEMM
+// accumulated: written once per block by its first CTA instead of summed per element.
 template <int DTYPE>
 __global__ void __launch_bounds__(kElemThreads)
 apply_update_kernel(const muzo_segment* __restrict__ segs, int nsegs, const float* __restrict__ scales,
@@ -238,46 +278,34 @@ apply_update_kernel(const muzo_segment* __restrict__ segs, int nsegs, const floa
     st[MUZO_STAT_RATIO_BEFORE] = sc.ratio;
     st[MUZO_STAT_CLIP_FACTOR] = sc.clip;
     st[MUZO_STAT_ZEROED] = sc.zeroed ? 1.0f : 0.0f;
+    const double c = sc.clipped ? static_cast<double>(sc.clip) : 1.0;
+    bs[MUZO_SUM_U2_CLIPPED] = sc.zeroed ? 0.0 : c * c * bs[MUZO_SUM_U2];
   }
   const bool vec = aligned16(v.out) && aligned16(v.param);
-  double acc = 0.0;
 #pragma unroll 1
   for (int it = 0; it < kItemsPerThread; ++it) {
     const int64_t item = v.local_item0 + it * kElemThreads + threadIdx.x;
     const int64_t li = item * 8;
     if (li >= v.numel) break;
-    const int cnt = li + 8 <= v.numel ? 8 : static_cast<int>(v.numel - li);
     float x[8], w[8];
-    if (vec && cnt == 8) {
+    if (vec && li + 8 <= v.numel) {
       load8(v.out, li, MUZO_BF16, x);
       load8(v.param, li, DTYPE, w);
+      apply8<DTYPE>(x, w, sc, scale, neg_lr, apply_decay, decay);
+      store8(v.param, li, DTYPE, w);
     } else {
+      const int cnt = static_cast<int>(v.numel - li < 8 ? v.numel - li : 8);
+#pragma unroll
       for (int k = 0; k < 8; ++k) {
         x[k] = k < cnt ? load_elem(v.out, li + k, MUZO_BF16) : 0.0f;
         w[k] = k < cnt ? load_elem(v.param, li + k, DTYPE) : 0.0f;
       }
-    }
-    float p = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float u = sc.zeroed ? 0.0f : x[k] * scale;       // U.mul_(sqrt(max)*muon_scale)
-      if (sc.clipped) u = u * sc.clip;                  // U.mul_(clip / ratio)
-      if (k < cnt) p = __fmaf_rn(u, u, p);
-      const float ud = round_to(u, DTYPE);              // U.to(block.dtype)
-      float nw = round_to(__fmaf_rn(neg_lr, ud, w[k]), DTYPE);  // block.add_(U, alpha=-lr)
-      if (apply_decay) nw = round_to(nw * decay, DTYPE);        // block.mul_(1 - lr*wd)
-      w[k] = nw;
-    }
-    acc += p;
-    if (vec && cnt == 8) store8(v.param, li, DTYPE, w);
-    else {
+      apply8<DTYPE>(x, w, sc, scale, neg_lr, apply_decay, decay);
 #pragma unroll
       for (int k = 0; k < 8; ++k)  // static indices keep w in registers
         if (k < cnt) store_elem(v.param, li + k, DTYPE, w[k]);
     }
   }
-  const double tot = block_sum(acc);
-  if (threadIdx.x == 0 && tot != 0.0) atomicAdd(bs + MUZO_SUM_U2_CLIPPED, tot);
 }
 
 // ------------------------------------------------------------------ QK-Clip row scaling

@@ -536,3 +536,31 @@ def test_step_hyperparameter_edges_match_exact_iteration(device, kw):
     assert stats["updated_param_count"] == len(captured) == 2
     errs = _check_against_exact(opt, before, captured, "normal", stats["lr"], dict(model.named_parameters()))
     print(kw, {k[0]: round(v, 4) for k, v in errs.items()})
+
+
+def test_normalize_is_the_ieee_quotient_bit_for_bit(device):
+    """X <- bf16(X / d) (newton_schulz.py:46-53) through the reciprocal product with the division
+    fallback near bf16 rounding midpoints: every element equal to torch's IEEE quotient rounded
+    to bf16, including the elements whose product lands near a midpoint."""
+    L = _lib()
+    g = torch.Generator(device="cpu").manual_seed(17)
+    x = (torch.randn((2048, 1031), generator=g) * 3.0).to(torch.bfloat16).to(device)
+    x[0, :8] = 0.0
+    sums = torch.zeros(L.NSUMS, dtype=torch.float64, device=device)
+    sums[L.SUM_X2] = float(x.double().square().sum())
+    sums[L.SUM_M2] = float(sums[L.SUM_X2])
+    denom = np.float32(np.float32(np.sqrt(float(sums[L.SUM_X2]))) + np.float32(1e-7))
+    want = (x.float() / torch.tensor(float(denom), device=device)).to(torch.bfloat16)
+    # elements whose reciprocal product lies within 4 fp32 ulps of a bf16 midpoint take the division
+    q = x.float() * torch.tensor(float(np.float32(1.0) / denom), device=device)
+    low = q.view(torch.int32) & 0xFFFF
+    assert int(((low - 0x7FFC >= 0) & (low - 0x7FFC <= 8)).sum()) > 0
+    out = x.clone()
+    segs, total = L.plan_linear([out.numel()], [out.data_ptr()], [out.data_ptr()])
+    table = L.to_device_table(segs, device)
+    flags = torch.zeros(4, dtype=torch.int32, device=device)
+    L.check(L.lib.muzo_ns_normalize(table.data_ptr(), len(segs), total, sums.data_ptr(), flags.data_ptr(),
+                                    L.stream_ptr(device)), "normalize")
+    torch.cuda.synchronize()
+    assert torch.equal(out, want), int((out != want).sum())
+    assert int(flags[0]) == 0
