@@ -249,8 +249,11 @@ class QKClipController:
     def reduce_over_group(self) -> None:
         """Replace the captured maxima by their maximum over the process group (every rank must
         call this together). Ranks may have captured different modules: a module captured on any
-        rank is present on all afterwards. Two all-reduces: the head count per module, then the
-        packed maxima (-inf where a rank has none)."""
+        rank is present on all afterwards. Two all-reduces: the head counts per module (their
+        maximum and, negated, their minimum over the ranks that captured the module, in one
+        tensor), then the packed maxima (-inf where a rank has none). Ranks that disagree on a
+        module's head count all raise the same ValueError after the first all-reduce, so no rank
+        is left waiting in the second."""
         pg = self.process_group
         if pg is None or not self._installed:
             return
@@ -261,16 +264,20 @@ class QKClipController:
         names = list(self.modules)  # named_modules order: identical on identical replicas
         first = next(iter(self.modules.values()))
         device = first.q_proj.weight.device
-        counts = torch.tensor([self._captured_smax[n].numel() if n in self._captured_smax else 0 for n in names],
+        big = 1 << 40  # stands for "not captured" in the minimum
+        have = [self._captured_smax[n].numel() if n in self._captured_smax else None for n in names]
+        counts = torch.tensor([c if c is not None else 0 for c in have] + [-(c if c is not None else big) for c in have],
                               dtype=torch.int64, device=device)
         dist.all_reduce(counts, op=dist.ReduceOp.MAX, group=pg)
-        sizes = [int(c) for c in counts.tolist()]
+        both = [int(c) for c in counts.tolist()]
+        sizes, smallest = both[:len(names)], [-c for c in both[len(names):]]
+        for name, hi, lo in zip(names, sizes, smallest):
+            if lo != big and lo != hi:   # every rank sees the same counts and raises alike
+                raise ValueError(f"QK-Clip capture of {name}: {lo} heads on one rank, {hi} on another")
         packed = torch.full((max(sum(sizes), 1),), float("-inf"), dtype=torch.float32, device=device)
         off = 0
         for name, k in zip(names, sizes):
             mine = self._captured_smax.get(name)
-            if mine is not None and mine.numel() != k:
-                raise ValueError(f"QK-Clip capture of {name}: {mine.numel()} heads on this rank, {k} on another")
             if mine is not None:
                 packed[off: off + k].copy_(mine.reshape(-1))
             off += k

@@ -163,8 +163,12 @@ def test_peer_destinations_open_each_handle_once():
 
 
 def _qk_worker(rank: int, world: int, store: str, out_dir: str) -> None:
+    from datetime import timedelta
+
     sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
-    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=world)
+    # a short timeout: a rank left waiting in a collective fails the test instead of hanging it
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=30))
     try:
         from muzo_clip_b200.qk_clip import QKClipController
 
@@ -189,7 +193,16 @@ def _qk_worker(rank: int, world: int, store: str, out_dir: str) -> None:
         # nothing captured anywhere: stays empty on every rank
         ctl.clear()
         ctl.reduce_over_group()
-        Path(out_dir, f"qk{rank}.txt").write_text(f"{int(got == want)} {int(not ctl._captured_smax)}\n")
+        empty = not ctl._captured_smax
+        # head counts that differ between the ranks: every rank raises, none is left waiting
+        ctl._captured_smax["layers.1"] = torch.zeros(4 if rank == 0 else 3)
+        try:
+            ctl.reduce_over_group()
+            raised = False
+        except ValueError:
+            raised = True
+        dist.barrier()   # the group still works afterwards
+        Path(out_dir, f"qk{rank}.txt").write_text(f"{int(got == want)} {int(empty)} {int(raised)}\n")
     finally:
         dist.destroy_process_group()
 
@@ -199,7 +212,7 @@ def test_qk_clip_maxima_reduced_over_two_gloo_ranks(tmp_path):
     mp.start_processes(_qk_worker, args=(world, str(tmp_path / "store"), str(tmp_path)), nprocs=world,
                        start_method="spawn")
     for r in range(world):
-        assert Path(tmp_path, f"qk{r}.txt").read_text().split() == ["1", "1"], r
+        assert Path(tmp_path, f"qk{r}.txt").read_text().split() == ["1", "1", "1"], r
 
 
 def test_collective_order_is_global_for_any_ownership():
@@ -210,3 +223,57 @@ def test_collective_order_is_global_for_any_ownership():
 
     src = Path(StepEngine.run_step.__code__.co_filename).read_text()
     assert "while next_class < len(self.class_order)" in src
+
+
+def _stall_worker(rank: int, world: int, store: str, out_dir: str) -> None:
+    import time
+    from datetime import timedelta
+
+    sys.path.insert(0, str(ROOT / "muzo-clip_b200"))
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=4))
+    try:
+        if rank == 1:
+            time.sleep(12)   # never joins the projection's loss all-reduce
+            return
+        import muzo_clip_b200.muzo_optimizer as mo
+
+        class FakeEngine:
+            def __init__(self, opt, *a, **k):
+                self.device = torch.device("cpu")
+
+            def matches(self, opt):
+                return True
+
+            def perturb(self, seed, alpha):
+                pass
+
+        mo.MuZOClipOptimizer._engine_for_step = lambda self: self._engine or setattr(self, "_engine", FakeEngine(self)) or self._engine
+        model = torch.nn.Module()
+        model.q_proj = torch.nn.Linear(8, 8, bias=False)
+        opt = mo.MuZOClipOptimizer(model, seed=3, process_group=dist.group.WORLD)
+        t0 = time.monotonic()
+        try:
+            opt.estimate_projection(lambda: 1.0)
+            outcome = "returned"
+        except Exception as exc:  # the collective's timeout error of the backend
+            outcome = type(exc).__name__
+        waited = time.monotonic() - t0
+        Path(out_dir, "stall.txt").write_text(f"{outcome} {waited:.1f} {len(opt.history)}\n")
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_stalled_rank_ends_the_others_collective_with_an_error(tmp_path):
+    """A rank that stops answering (here: never joins the SPSA loss all-reduce that ends a
+    projection) makes the other rank's collective fail within the process group's timeout
+    (4 s) instead of waiting for ever; the projection then raises and appends nothing to the
+    history (muzo_optimizer.py:213-215 re-raises exceptions of a projection)."""
+    world = 2
+    mp.start_processes(_stall_worker, args=(world, str(tmp_path / "store"), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    outcome, waited, hist = Path(tmp_path, "stall.txt").read_text().split()
+    assert outcome != "returned" and float(waited) < 11.0 and hist == "0", (outcome, waited, hist)
