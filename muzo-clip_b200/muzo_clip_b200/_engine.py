@@ -446,6 +446,12 @@ class StepEngine:
             self._phase_events = None
 
     def _mark(self, phase: str, start: bool, stream=None) -> None:
+        """Phase boundary: an NVTX range (muzo/<phase>) for profilers and, while phase timing is
+        on, a CUDA event on the phase's stream."""
+        if start:
+            torch.cuda.nvtx.range_push(f"muzo/{phase}")
+        else:
+            torch.cuda.nvtx.range_pop()
         ev_map = getattr(self, "_phase_events", None)
         if ev_map is None:
             return

@@ -95,6 +95,7 @@ class PeerExchange:
         """Queue the copies of `blocks` (final on this rank once `ready` has passed) to every peer."""
         if not blocks:
             return
+        torch.cuda.nvtx.range_push("muzo/push")
         src = np.asarray([b.tensor.data_ptr() for b in blocks], dtype=np.uint64)
         nbytes = np.asarray([b.numel * b.tensor.element_size() for b in blocks], dtype=np.uint64)
         for r, stream in self.streams.items():
@@ -102,6 +103,7 @@ class PeerExchange:
             dst = np.asarray([self.dst[r][b.index] for b in blocks], dtype=np.uint64)
             _lib.launch("muzo_push_blocks", dst.ctypes.data, src.ctypes.data, nbytes.ctypes.data, len(blocks),
                         stream.cuda_stream)
+        torch.cuda.nvtx.range_pop()
 
     def join(self, stream: torch.cuda.Stream) -> None:
         """Make `stream` wait for every push queued so far."""
@@ -205,6 +207,8 @@ class ShardedStepEngine(StepEngine):
             if pending:
                 self._handles.append(self._broadcast(self._class_blocks(pending)))
         compute = torch.cuda.current_stream(self.device) if self.device.type == "cuda" else None
+        if compute is not None:
+            self._mark("exchange", True)
         self.scatter_owned_results()
         if compute is not None:
             self.comm_stream.wait_stream(compute)
@@ -213,6 +217,7 @@ class ShardedStepEngine(StepEngine):
             with torch.cuda.stream(self.comm_stream):
                 self.reduce_results()
             compute.wait_stream(self.comm_stream)
+            self._mark("exchange", False)
         else:
             self.reduce_results()
         handles, self._handles = self._handles, []
