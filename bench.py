@@ -152,10 +152,12 @@ class ClockSampler:
 
 # DRAM traffic measured by one ncu capture of this workload on one B200 (1-pass metrics
 # gpu__time_duration.sum, dram__bytes_read.sum, dram__bytes_write.sum, --clock-control none, on
-# `python bench.py --steps 1 --warmup 1 --no-cpu-baseline`): read + write summed over the 105
-# ns_gemm launches of one step (794.4 GB over the 2 captured steps), and per perturbation pass.
-NS_DRAM_BYTES_PER_STEP = 397.2e9
-PERTURB_DRAM_BYTES_PER_PASS = 27.89e9
+# `python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-variant`): read + write of the
+# timed step, summed over its 105 ns_gemm launches, per perturbation pass and for the rebuild.
+NS_DRAM_BYTES_PER_STEP = 398.4e9
+PERTURB_DRAM_BYTES_PER_PASS = 27.89e9          # a pass that regenerates its noise
+PERTURB_KEPT_DRAM_BYTES_PER_PASS = 41.92e9     # mean of the keeping pass and the two kept passes
+REBUILD_KEPT_DRAM_BYTES_PER_STEP = 139.52e9
 TRAFFIC_SOURCE = "profiles/launches_dram_llama3_8b_step.md (one ncu capture, not measured in this run)"
 
 
@@ -356,6 +358,7 @@ def run_gpu(args) -> int:
                 "bound": "hbm", "kernel": "rebuild_kept_linear_kernel", "achieved": gbs(moved, rebuild_ms),
                 "unit": "GB/s", "peak": hbm, "frac": round(gbs(moved, rebuild_ms) / hbm, 4),
                 "bytes": moved, "bytes_note": "2H + 4 B per weight actually moved (H kept noise entries read)",
+                "traffic": REBUILD_KEPT_DRAM_BYTES_PER_STEP if world == 1 else None, "traffic_source": TRAFFIC_SOURCE,
                 "algorithmic_bytes": rebuild_bytes, "algorithmic_achieved": gbs(rebuild_bytes, rebuild_ms),
                 "algorithmic_frac": round(gbs(rebuild_bytes, rebuild_ms) / hbm, 4)}
         else:
@@ -415,7 +418,8 @@ def run_gpu(args) -> int:
                 "moved_gbs": gbs(perturb_moved, 3.0 * perturb_ms),
                 "moved_frac": round(gbs(perturb_moved, 3.0 * perturb_ms) / hbm, 4),
                 "rademacher_achieved": round(rad_gbs, 1), "rademacher_frac": round(rad_gbs / hbm, 4),
-                "traffic": PERTURB_DRAM_BYTES_PER_PASS, "traffic_unit": "DRAM bytes per regenerating pass",
+                "traffic": PERTURB_KEPT_DRAM_BYTES_PER_PASS if run["keep_noise"] else PERTURB_DRAM_BYTES_PER_PASS,
+                "traffic_unit": "DRAM bytes per pass (mean of the step's three)",
                 "traffic_source": TRAFFIC_SOURCE, "algorithmic_bytes": perturb_bytes,
             },
             "rebuild_roofline": rebuild_roofline,
@@ -657,6 +661,34 @@ def _run_one_case(args) -> int:
                    horizon=args.horizon if args.case == "rebuild" else None,
                    ms=round(ms, 4), gbs=round(gbs, 1), hbm_frac=round(gbs / peaks["hbm_gbs"], 4),
                    l2="flushed between passes" if flush is not None else "working set larger than L2")
+    elif args.case == "attn":
+        # one attention layer with the per-head max-logit side output (the fused capture path)
+        # against SDPA plus the separate max-logit kernel on the same states
+        from muzo_clip_b200 import _qk
+
+        b, hq, hkv, seq, d = args.batch, args.heads, args.kv_heads, args.seq, args.head_dim
+        q = torch.randn((b, seq, hq, d), device=device, dtype=torch.bfloat16).transpose(1, 2)
+        k = torch.randn((b, seq, hkv, d), device=device, dtype=torch.bfloat16).transpose(1, 2)
+        v = torch.randn((b, seq, hkv, d), device=device, dtype=torch.bfloat16).transpose(1, 2)
+        fused = lambda: _qk.attention_max(q, k, v, d ** -0.5, True)  # noqa: E731
+
+        def separate():
+            torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, scale=d ** -0.5,
+                                                             enable_gqa=True)
+            _qk.qk_head_max(q, k, d ** -0.5, True, None)
+
+        sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(  # noqa: E731
+            q, k, v, is_causal=True, scale=d ** -0.5, enable_gqa=True)
+        res = {}
+        for name, fn in (("fused", fused), ("sdpa_plus_max", separate), ("sdpa", sdpa)):
+            for _ in range(args.warmup):
+                fn()
+            res[name] = _event_ms(fn, args.steps, stream)
+        flops = 4.0 * b * hq * seq * seq * d / 2.0  # Q K^T and P V, causal half
+        out.update(batch=b, heads=hq, kv_heads=hkv, seq=seq, head_dim=d,
+                   ms_fused=round(res["fused"], 4), ms_sdpa_plus_max=round(res["sdpa_plus_max"], 4),
+                   ms_sdpa=round(res["sdpa"], 4), fused_tflops=round(flops / res["fused"] / 1e9, 1),
+                   sdpa_tflops=round(flops / res["sdpa"] / 1e9, 1))
     elif args.case == "qk":
         # per-head max logit of one attention layer: Q [B, Hq, S, D], K [B, Hkv, S, D] as the
         # transposed views of [B, S, H, D] that transformers passes to attention functions
@@ -680,7 +712,7 @@ def _run_one_case(args) -> int:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", default=None, choices=["ns", "perturb", "rebuild", "apply", "normalize", "qk"],
+    ap.add_argument("--case", default=None, choices=["ns", "perturb", "rebuild", "apply", "normalize", "qk", "attn"],
                     help="run one kernel family on a small workload instead of the optimizer step")
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)

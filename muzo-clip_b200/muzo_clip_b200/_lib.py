@@ -105,6 +105,10 @@ _SIGNATURES = {
     "muzo_logits_head_max": ([_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp], _i32),
     "muzo_max_merge": ([_vp, _vp, _vp, _i64, _vp], _i32),
     "muzo_ns_normalize_noalloc": ([_vp, _vp, _vp, _i32, _i32, _vp, _vp], _i32),
+    "muzo_attention_max": (
+        [_vp, _vp, _vp, _vp, _i32] + [_i64] * 6 + [_i64] * 12 + [_i32, _f32, _vp, _vp, _vp, _vp, _vp, _vp],
+        _i32,
+    ),
     "muzo_ipc_export": ([_vp, _vp, _vp, _vp], _i32),
     "muzo_ipc_import": ([_vp, _vp], _i32),
     "muzo_ipc_close": ([_vp], _i32),
@@ -130,7 +134,7 @@ KERNELS_PER_CALL = {
     "muzo_ns_prepare": 1, "muzo_rebuild_segments_history": 1, "muzo_rebuild_kept_linear": 1,
     "muzo_ns_normalize": 1, "muzo_ns_gemm": 1, "muzo_update_sumsq": 1, "muzo_apply_update": 1,
     "muzo_qk_scale_rows": 1, "muzo_qk_max": 3, "muzo_logits_head_max": 3, "muzo_max_merge": 1,
-    "muzo_ns_normalize_noalloc": 3, "muzo_ipc_export": 0, "muzo_ipc_import": 0, "muzo_ipc_close": 0,
+    "muzo_ns_normalize_noalloc": 3, "muzo_attention_max": 3, "muzo_ipc_export": 0, "muzo_ipc_import": 0, "muzo_ipc_close": 0,
     "muzo_push_blocks": 0,
 }
 launch_count = 0

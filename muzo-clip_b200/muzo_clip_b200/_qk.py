@@ -4,6 +4,7 @@ transformers calls during a probe forward, and the q/k row scaling."""
 from __future__ import annotations
 
 import contextvars
+import os
 import weakref
 
 import numpy as np
@@ -166,19 +167,105 @@ def scale_rows(weight: torch.Tensor, groups: int, rows_per_group: int, factors: 
                                     int(weight.shape[1]), fptr, mptr, _lib.stream_ptr(dev))
 
 
+# ---------------------------------------------------------------- fused attention
+
+_ATTN_STATUS: dict[int, torch.Tensor] = {}
+
+
+def attention_status(device: torch.device) -> torch.Tensor:
+    """One device int32 per GPU: the first nonzero timeout code of a fused attention launch."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _ATTN_STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _ATTN_STATUS[idx] = t
+    return t
+
+
+def check_attention_status(device: torch.device) -> None:
+    """Raise if a fused attention launch on `device` reported an expired wait (reads one word)."""
+    if device.type != "cuda" or not _ATTN_STATUS:
+        return
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _ATTN_STATUS.get(idx)
+    if t is not None and int(t.item()) != 0:
+        code = int(t.item())
+        t.zero_()
+        raise _lib.MuzoError(f"fused attention reported status {code} (a bounded wait expired); the outputs of "
+                             "the forward that ran it are unspecified")
+
+
+def fused_attention_eligible(query, key, value, dropout: float) -> bool:
+    """True when the tcgen05 attention kernel can take this call: bf16/fp16 CUDA states with head
+    dim 64 or 128, D contiguous, strides of multiples of 8 elements, 16-byte aligned bases, no
+    dropout and no gradient needed."""
+    if dropout or query.device.type != "cuda" or query.dtype not in (torch.bfloat16, torch.float16):
+        return False
+    if key.dtype != query.dtype or value.dtype != query.dtype or query.shape[-1] not in (64, 128):
+        return False
+    if torch.is_grad_enabled() and (query.requires_grad or key.requires_grad or value.requires_grad):
+        return False
+    if query.shape[1] % key.shape[1] != 0 or value.shape[:3] != key.shape[:3] or value.shape[-1] != query.shape[-1]:
+        return False
+    for t in (query, key, value):
+        if t.stride(-1) != 1 or any(int(st) % 8 for st in t.stride()[:3]) or t.data_ptr() % 16:
+            return False
+    return True
+
+
+def attention_max(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scaling: float, causal: bool,
+                  key_lo: torch.Tensor | None = None, key_hi: torch.Tensor | None = None,
+                  record: bool = True) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
+    """softmax(scaling * Q K^T) V on the tensor cores for Q [B, Hq, Sq, D], K, V [B, Hkv, Sk, D]
+    (transformers' transposed views), returned as [B, Sq, Hq, D] (the layout attention functions
+    return); with ``record``, also the per-head max of the eager pre-softmax logits and a validity
+    word, on the device. ``key_lo``/``key_hi`` (int32 per batch) bound the visible keys."""
+    b, hq, sq, d = (int(v) for v in query.shape)
+    hkv, sk = int(key.shape[1]), int(key.shape[2])
+    dev = query.device
+    out = torch.empty((b, sq, hq, d), dtype=query.dtype, device=dev)
+    smax = torch.empty(hq, dtype=torch.float32, device=dev) if record else None
+    valid = torch.empty(1, dtype=torch.int32, device=dev) if record else None
+    status = attention_status(dev)
+    _lib.launch("muzo_attention_max", query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+                _lib.dtype_code(query.dtype), b, hq, hkv, sq, sk, d,
+                query.stride(0), query.stride(1), query.stride(2), key.stride(0), key.stride(1), key.stride(2),
+                value.stride(0), value.stride(1), value.stride(2), sq * hq * d, d, hq * d,
+                1 if causal else 0, float(scaling),
+                key_lo.data_ptr() if key_lo is not None else None, key_hi.data_ptr() if key_hi is not None else None,
+                smax.data_ptr() if smax is not None else None, valid.data_ptr() if valid is not None else None,
+                status.data_ptr(), _lib.stream_ptr(dev))
+    return out, smax, valid
+
+
 # ---------------------------------------------------------------- probe attention
 
 
 def _probe_attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
-    """Attention function of the probe and of training-time capture: SDPA computes the output
-    (and its backward); while a QK-Clip capture is active, the library's max-logit kernel reads
-    the same post-RoPE query and key states and records the per-head max of the pre-softmax
-    logits. Outside a capture it is SDPA alone."""
+    """Attention function of the probe and of training-time capture. While a QK-Clip capture is
+    active and the call qualifies (bf16/fp16, head dim 64 or 128, no gradient, no mask or the
+    plain causal mask), one tensor-core kernel computes the attention output and the per-head
+    max of the pre-softmax logits together (Q K^T formed once); otherwise SDPA computes the
+    output (and its backward) and, during a capture, the library's max-logit kernel reads the
+    same post-RoPE query and key states. Outside a capture it is SDPA alone."""
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
 
     ctrl = _ACTIVE.get()
     if scaling is None:
         scaling = query.shape[-1] ** -0.5
+    if ctrl is not None and os.environ.get("MUZO_FUSED_ATTENTION", "1") != "0":
+        # one kernel for the attention and the capture when the call qualifies: no mask (the
+        # module's causality) or the plain causal mask
+        mask = attention_mask if attention_mask is not None and attention_mask.ndim == 4 else None
+        sq = query.shape[2]
+        plain = mask is None or _is_plain_causal(mask, sq, key.shape[2])
+        name = ctrl.module_name(module)
+        if name is not None and plain and fused_attention_eligible(query, key, value, dropout):
+            causal = True if mask is not None else bool(getattr(module, "is_causal", True)) and sq > 1
+            with torch.no_grad():
+                out, smax, valid = attention_max(query, key, value, float(scaling), causal)
+            ctrl.record_max(name, smax, valid)
+            return out, None
     if ctrl is not None:
         with torch.no_grad():
             sq = query.shape[2]

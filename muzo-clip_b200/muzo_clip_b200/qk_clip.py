@@ -166,6 +166,17 @@ class QKClipController:
         per_head, valid = _qk.qk_head_max(query, key, scaling, causal, attention_mask)
         self._record(name, per_head, valid)
 
+    def module_name(self, module: torch.nn.Module) -> str | None:
+        """The capture name of an attention module (or of the innermost one being run)."""
+        name = self._names_by_id.get(id(module))
+        if name is None and self._module_stack:
+            name = self._module_stack[-1]
+        return name
+
+    def record_max(self, name: str, per_head: torch.Tensor, valid: torch.Tensor) -> None:
+        """Per-head maxima an attention kernel computed as a side output (fused capture path)."""
+        self._record(name, per_head, valid)
+
     @contextlib.contextmanager
     def capture(self) -> Iterator[None]:
         """Record pre-softmax maxima during forward calls (softmax capture + probe attention)."""
@@ -302,6 +313,7 @@ class QKClipController:
             return QKClipApplyStats(False, False, False, reason, 0.0, 0)
 
         names = list(self._captured_smax)
+        _qk.check_attention_status(self._captured_smax[names[0]].device)
         host = _qk.to_host([self._captured_smax[n] for n in names])  # one device-to-host copy
         fallback_used = False
         clip_count = 0

@@ -538,23 +538,40 @@ def test_step_hyperparameter_edges_match_exact_iteration(device, kw):
     print(kw, {k[0]: round(v, 4) for k, v in errs.items()})
 
 
+def _denominator_with_midpoint_products(seed: int = 5) -> float:
+    """A sum of squares whose normalisation denominator d makes the reciprocal product x * (1/d)
+    of some bf16 mantissa land within 4 fp32 ulps of a bf16 rounding midpoint (so the division
+    fallback runs): with one denominator the products take only 128 mantissa patterns."""
+    rng = np.random.default_rng(seed)
+    ks = ((128 + np.arange(128)) / 128.0).astype(np.float32)   # bf16 mantissas in [1, 2)
+    for _ in range(100000):
+        s2 = float(rng.uniform(1e2, 1e6))
+        d = np.float32(np.float32(np.sqrt(s2)) + np.float32(1e-7))
+        q = (ks * (np.float32(1.0) / d)).astype(np.float32)
+        low = (q.view(np.uint32) & 0xFFFF).astype(np.int64)
+        if np.any((low >= 0x7FFC) & (low <= 0x8004)):
+            return s2
+    raise AssertionError("no denominator found")
+
+
 def test_normalize_is_the_ieee_quotient_bit_for_bit(device):
     """X <- bf16(X / d) (newton_schulz.py:46-53) through the reciprocal product with the division
     fallback near bf16 rounding midpoints: every element equal to torch's IEEE quotient rounded
-    to bf16, including the elements whose product lands near a midpoint."""
+    to bf16, with a denominator for which some products do land near a midpoint."""
     L = _lib()
     g = torch.Generator(device="cpu").manual_seed(17)
     x = (torch.randn((2048, 1031), generator=g) * 3.0).to(torch.bfloat16).to(device)
     x[0, :8] = 0.0
+    s2 = _denominator_with_midpoint_products()
     sums = torch.zeros(L.NSUMS, dtype=torch.float64, device=device)
-    sums[L.SUM_X2] = float(x.double().square().sum())
-    sums[L.SUM_M2] = float(sums[L.SUM_X2])
-    denom = np.float32(np.float32(np.sqrt(float(sums[L.SUM_X2]))) + np.float32(1e-7))
+    sums[L.SUM_X2] = s2
+    sums[L.SUM_M2] = s2
+    denom = np.float32(np.float32(np.sqrt(s2)) + np.float32(1e-7))
     want = (x.float() / torch.tensor(float(denom), device=device)).to(torch.bfloat16)
     # elements whose reciprocal product lies within 4 fp32 ulps of a bf16 midpoint take the division
     q = x.float() * torch.tensor(float(np.float32(1.0) / denom), device=device)
     low = q.view(torch.int32) & 0xFFFF
-    assert int(((low - 0x7FFC >= 0) & (low - 0x7FFC <= 8)).sum()) > 0
+    assert int(((low >= 0x7FFC) & (low <= 0x8004)).sum()) > 0
     out = x.clone()
     segs, total = L.plan_linear([out.numel()], [out.data_ptr()], [out.data_ptr()])
     table = L.to_device_table(segs, device)
