@@ -30,7 +30,7 @@ using namespace tc;
 constexpr int AM = 128;          // query rows per CTA (UMMA M)
 constexpr int AN = 128;          // keys per tile: UMMA N of S, the K of P V
 constexpr int ABK = 64;          // 128-byte swizzle row of 16-bit elements
-constexpr int A_THREADS = 192;
+constexpr int A_THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 softmax (two per TMEM lane quarter)
 constexpr int KV_STAGES = 2;
 constexpr int SUB_BYTES = 128 * ABK * 2;     // one swizzled block of 128 rows x 64 elements (16 KB)
 constexpr int BOX_BYTES = 64 * ABK * 2;      // one 64 x 64 box of the MN-major V operand (8 KB)
@@ -45,8 +45,10 @@ struct AttnLayout {
   static constexpr int P_BYTES = 2 * SUB_BYTES;
   static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
   static constexpr int TILES_BYTES = Q_BYTES + KV_STAGES * STAGE_BYTES + P_BYTES;
-  // at least 116 KB so that one CTA holds an SM: every CTA allocates all 512 TMEM columns
-  static constexpr int SMEM_BYTES = TILES_BYTES + 1024 + 512 > 116 * 1024 ? TILES_BYTES + 1024 + 512 : 116 * 1024;
+  // tiles, 1 KB of barriers and flags, 3 KB + 96 B of softmax exchange, 1 KB of alignment; at
+  // least 116 KB so that one CTA holds an SM (every CTA allocates all 512 TMEM columns)
+  static constexpr int NEED = TILES_BYTES + 1024 + 6 * AM * 4 + 24 * 4 + 1024;
+  static constexpr int SMEM_BYTES = NEED > 116 * 1024 ? NEED : 116 * 1024;
 };
 
 struct AttnArgs {
@@ -126,6 +128,11 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   uint64_t* drain = o_done + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
+  // softmax pair exchange: row maxima [2 tile parities][2 halves][128 rows], then the row sums
+  // [2 halves][128 rows]; each warp's "still running" word [2 parities][2 halves][4 quarters],
+  // then the final one [2 halves][4 quarters]
+  float* red_max = reinterpret_cast<float*>(smem + L::TILES_BYTES + 1024);
+  int* red_ok = reinterpret_cast<int*>(red_max + 6 * AM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b, h, qb;
@@ -138,8 +145,8 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < KV_STAGES; ++s) { mbar_init(kv_full + s, 1); mbar_init(kv_empty + s, 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(s_full + s, 1); mbar_init(s_empty + s, 4); }
-    mbar_init(p_full, 4);
+    for (int s = 0; s < 2; ++s) { mbar_init(s_full + s, 1); mbar_init(s_empty + s, 8); }
+    mbar_init(p_full, 8);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -247,61 +254,76 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax and epilogue
+    // Two warps per TMEM lane quarter: warp half h takes keys [64 h, 64 h + 64) of every tile,
+    // and columns [h D/2, (h + 1) D/2) of O. The pair exchanges its row maxima once per tile
+    // through shared memory (named barrier 1 + quarter, 64 threads).
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = 32 * quarter + lane;                 // row of the block == TMEM lane
     const int64_t row = static_cast<int64_t>(qb) * AM + r;
     const bool row_in = row < g.sq;
     const int64_t jmax = g.causal ? row + g.shift : g.sk - 1;  // last key visible by causality
     const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
+    constexpr int HN = AN / 2;         // keys per warp and tile
+    constexpr int HD = D / 2;          // O columns per warp
     float m_run = -INFINITY;    // running maximum of the scaled logits (log2 units) used by P
-    float l_run = 0.0f;         // running sum of P
+    float l_run = 0.0f;         // running sum of this warp's half of P
     float raw_max = -INFINITY;  // side output: maximum of the visible raw logits q . k
     bool finite = true;
     bool ok = true;
-    for (int j = 0; j < ntiles && ok; ++j) {
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory"); };
+    // The pair leaves the loop together: every failure (an expired wait, an abort) is noted in
+    // `ok` and exchanged at the next per-tile barrier (or the final one), never acted on alone.
+    for (int j = 0; j < ntiles; ++j) {
       const int sb = j & 1;
       const uint32_t sp = static_cast<uint32_t>((j >> 1) & 1);
-      bool ready = true;
-      if (lane == 0) ready = mbar_wait(s_full + sb, sp);
+      bool ready = ok;
+      if (lane == 0 && ready) ready = mbar_wait(s_full + sb, sp);
       ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
-      if (!ready || *reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      float s[AN];
+      ready = ready && !*reinterpret_cast<volatile int*>(abort_flag);
+      red_ok[(j & 1) * 8 + half * 4 + quarter] = ready ? 1 : 0;
+      float s[HN];
+      if (ready) {
+        tc_fence_after();
+        uint32_t v[HN];
+        tmem_ld64(tmem_base + lane_addr + sb * AN + half * HN, v);
 #pragma unroll
-      for (int c = 0; c < AN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem_base + lane_addr + sb * AN + c * 32, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(v[e]);
+        for (int e = 0; e < HN; ++e) s[e] = __uint_as_float(v[e]);
+        tc_fence_before();
       }
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty + sb);       // S buffer free for S_{j+2}
-      // visibility of this tile's keys for this row
-      const int64_t key0 = static_cast<int64_t>(t0 + j) * AN;
-      const bool all_visible = row_in && key0 >= lo && key0 + AN <= hi && key0 + AN - 1 <= jmax;
-      float mt = -INFINITY;
+      if (lane == 0 && ready) mbar_arrive(s_empty + sb);  // S buffer (this half) free for S_{j+2}
+      // visibility of this half tile's keys for this row; partial maxima and the non-finite test
+      const int64_t key0 = static_cast<int64_t>(t0 + j) * AN + half * HN;
+      const bool all_visible = row_in && key0 >= lo && key0 + HN <= hi && key0 + HN - 1 <= jmax;
+      float mp[8];
+      uint32_t badp[8];   // a visible logit with all exponent bits set: +-inf or NaN
+#pragma unroll
+      for (int q = 0; q < 8; ++q) { mp[q] = -INFINITY; badp[q] = 0u; }
       if (all_visible) {
 #pragma unroll
-        for (int c = 0; c < AN; ++c) {
-          finite = finite && isfinite(s[c]);
-          mt = fmaxf(mt, s[c]);
-        }
+        for (int c = 0; c < HN; ++c) badp[c & 7] |= (__float_as_uint(s[c]) & 0x7fffffffu) >= 0x7f800000u ? 1u : 0u;
       } else {
+        const int64_t vis_lo = lo - key0, vis_hi_excl = (hi < jmax + 1 ? hi : jmax + 1) - key0;
 #pragma unroll
-        for (int c = 0; c < AN; ++c) {
-          const int64_t key = key0 + c;
-          const bool vis = row_in && key >= lo && key < hi && key <= jmax;
-          if (vis) {
-            finite = finite && isfinite(s[c]);
-            mt = fmaxf(mt, s[c]);
-          } else {
-            s[c] = -INFINITY;
-          }
+        for (int c = 0; c < HN; ++c) {
+          if (!row_in || c < vis_lo || c >= vis_hi_excl) s[c] = -INFINITY;
+          else badp[c & 7] |= (__float_as_uint(s[c]) & 0x7fffffffu) >= 0x7f800000u ? 1u : 0u;
         }
       }
-      raw_max = fmaxf(raw_max, mt);
-      // lazy online softmax in base 2
+#pragma unroll
+      for (int c = 0; c < HN; ++c) mp[c & 7] = fmaxf(mp[c & 7], s[c]);
+      const float mine = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      finite = finite && (badp[0] | badp[1] | badp[2] | badp[3] | badp[4] | badp[5] | badp[6] | badp[7]) == 0u;
+      raw_max = fmaxf(raw_max, mine);
+      // exchange the half-row maxima (double-buffered by tile parity)
+      red_max[((j & 1) * 2 + half) * AM + r] = mine;
+      pair_sync();
+      const float other = red_max[((j & 1) * 2 + (half ^ 1)) * AM + r];
+      const bool pair_ok = red_ok[(j & 1) * 8 + (half ^ 1) * 4 + quarter] != 0;
+      if (!ready || !pair_ok) { ok = false; break; }
+      const float mt = fmaxf(mine, other);
+      // lazy online softmax in base 2 (both halves reach the same m_run and alpha)
       const float mt2 = mt * g.scale_log2;
       float alpha = 1.0f;
       bool rescale = false;
@@ -310,57 +332,59 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         rescale = j > 0;
         m_run = mt2;
       }
-      float lsum = 0.0f;
-      uint32_t packed[AN / 2];
+      float lp[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) lp[q] = 0.0f;
+      uint32_t packed[HN / 2];
       if (m_run == -INFINITY) {
 #pragma unroll
-        for (int c = 0; c < AN / 2; ++c) packed[c] = 0u;
+        for (int c = 0; c < HN / 2; ++c) packed[c] = 0u;
       } else {
 #pragma unroll
-        for (int c = 0; c < AN; c += 2) {
+        for (int c = 0; c < HN; c += 2) {
           const float p0 = fast_exp2(fmaf(s[c], g.scale_log2, -m_run));
           const float p1 = fast_exp2(fmaf(s[c + 1], g.scale_log2, -m_run));
-          lsum += p0 + p1;
+          lp[(c >> 1) & 7] += p0 + p1;
           if (FMT == 1) packed[c / 2] = pack_bf16(p0, p1);
           else packed[c / 2] = pack_half(p0, p1);
         }
       }
+      const float lsum = ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
       l_run = l_run * alpha + lsum;
       // P V of the previous tile must be done: the P buffer is reused and O may be rescaled
       if (j > 0) {
         bool done = true;
         if (lane == 0) done = mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1));
         done = __shfl_sync(0xffffffffu, done ? 1 : 0, 0) != 0;
-        if (!done) { ok = false; break; }
+        if (!done) { ok = false; continue; }   // the next barrier ends the pair's loop
         tc_fence_after();
       }
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           uint32_t v[32];
-          tmem_ld32(tmem_o + lane_addr + c * 32, v);
+          tmem_ld32(tmem_o + lane_addr + half * HD + c * 32, v);
           if (rescale) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
           }
-          tmem_st32(tmem_o + lane_addr + c * 32, v);
+          tmem_st32(tmem_o + lane_addr + half * HD + c * 32, v);
         }
       }
-      // P row into the swizzled K-major layout: chunk c16 of 8 keys of block kb sits at
-      // row * 128 + ((c16 ^ (row & 7)) * 16)
+      // this half of the P row into K block `half` of the swizzled K-major layout: chunk c16 of
+      // 8 keys sits at row * 128 + ((c16 ^ (row & 7)) * 16)
 #pragma unroll
-      for (int g16 = 0; g16 < AN / 8; ++g16) {
-        const int kb = g16 >> 3, c16 = g16 & 7;
-        uint8_t* dst = sP + kb * SUB_BYTES + r * 128 + ((c16 ^ (r & 7)) << 4);
+      for (int c16 = 0; c16 < HN / 8; ++c16) {
+        uint8_t* dst = sP + half * SUB_BYTES + r * 128 + ((c16 ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) =
-            make_uint4(packed[4 * g16], packed[4 * g16 + 1], packed[4 * g16 + 2], packed[4 * g16 + 3]);
+            make_uint4(packed[4 * c16], packed[4 * c16 + 1], packed[4 * c16 + 2], packed[4 * c16 + 3]);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // epilogue: O / l of this row
+    // epilogue: O / l of this row, this warp's half of the columns
     if (ok && ntiles > 0) {
       bool done = true;
       if (lane == 0) done = mbar_wait(o_done, static_cast<uint32_t>((ntiles - 1) & 1));
@@ -368,14 +392,21 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       if (!done) ok = false;
       tc_fence_after();
     }
+    // the row sum is the two halves' sums (both warps of the pair reach this barrier together:
+    // a failed wait ends both loops at the same tile)
+    red_max[(4 + half) * AM + r] = l_run;
+    red_ok[16 + half * 4 + quarter] = ok;
+    pair_sync();
+    const float l_total = l_run + red_max[(4 + (half ^ 1)) * AM + r];
+    ok = ok && red_ok[16 + (half ^ 1) * 4 + quarter] != 0;
     if (ok) {
-      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      const float inv = l_total > 0.0f ? 1.0f / l_total : 0.0f;
       uint16_t* orow = reinterpret_cast<uint16_t*>(g.out) + static_cast<int64_t>(b) * g.o_sb +
-                       static_cast<int64_t>(h) * g.o_sh + row * g.o_ss;
+                       static_cast<int64_t>(h) * g.o_sh + row * g.o_ss + half * HD;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         uint32_t v[32];
-        if (ntiles > 0) tmem_ld32(tmem_o + lane_addr + c * 32, v);
+        if (ntiles > 0) tmem_ld32(tmem_o + lane_addr + half * HD + c * 32, v);
         else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = 0u;

@@ -242,20 +242,21 @@ def attention_max(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, s
 
 
 def _probe_attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
-    """Attention function of the probe and of training-time capture. While a QK-Clip capture is
-    active and the call qualifies (bf16/fp16, head dim 64 or 128, no gradient, no mask or the
-    plain causal mask), one tensor-core kernel computes the attention output and the per-head
-    max of the pre-softmax logits together (Q K^T formed once); otherwise SDPA computes the
-    output (and its backward) and, during a capture, the library's max-logit kernel reads the
-    same post-RoPE query and key states. Outside a capture it is SDPA alone."""
+    """Attention function of the probe and of training-time capture: SDPA computes the output
+    (and its backward); while a QK-Clip capture is active, the library's max-logit kernel reads
+    the same post-RoPE query and key states and records the per-head max of the pre-softmax
+    logits. With MUZO_FUSED_ATTENTION=1, a capture call that qualifies (bf16/fp16, head dim 64 or
+    128, no gradient, no mask or the plain causal mask) runs one tensor-core kernel for the
+    output and the maxima instead (Q K^T formed once). Outside a capture it is SDPA alone."""
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
 
     ctrl = _ACTIVE.get()
     if scaling is None:
         scaling = query.shape[-1] ** -0.5
-    if ctrl is not None and os.environ.get("MUZO_FUSED_ATTENTION", "1") != "0":
+    if ctrl is not None and os.environ.get("MUZO_FUSED_ATTENTION", "0") == "1":
         # one kernel for the attention and the capture when the call qualifies: no mask (the
-        # module's causality) or the plain causal mask
+        # module's causality) or the plain causal mask. Off by default: on one Llama-3-70B layer
+        # it takes 0.52 ms against 0.37 ms for SDPA plus the separate max-logit kernel
         mask = attention_mask if attention_mask is not None and attention_mask.ndim == 4 else None
         sq = query.shape[2]
         plain = mask is None or _is_plain_causal(mask, sq, key.shape[2])

@@ -182,13 +182,15 @@ def test_probe_reports_disabled_without_modules(device):
     assert st["enabled"] is False and st["disabled_reason"] == "no q_proj/k_proj attention modules found"
 
 
+@pytest.mark.parametrize("fused", ["0", "1"])
 @pytest.mark.parametrize("padded", [False, True])
-def test_training_capture_attention(device, padded):
+def test_training_capture_attention(device, monkeypatch, padded, fused):
     """use_qk_capture_attention: outputs and gradients are SDPA's; the clean forward of
     estimate_projection (qk_capture_clean_forward=True) records the eager maxima exactly, with
     and without a padding mask; apply_qk_clip_if_available then clips."""
     from muzo_clip_b200 import MuZOClipOptimizer, use_qk_capture_attention
 
+    monkeypatch.setenv("MUZO_FUSED_ATTENTION", fused)   # SDPA + max kernel, or the fused attention kernel
     model = _tiny_llama(torch.bfloat16, device)
     with torch.no_grad():
         model.model.layers[0].self_attn.q_proj.weight.mul_(40.0)
