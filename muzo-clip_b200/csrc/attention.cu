@@ -2,17 +2,20 @@
 // side output: QK-Clip's capture (qk_clip.py:173-196) computed by the attention that the forward
 // runs anyway, so Q K^T is formed once. Forward only (MuZO's forwards run without gradients).
 //
-// One CTA per (batch, query head, block of 128 queries), 6 warps:
-//   warp 0      TMA producer (one thread): the Q block once, then K and V tiles of 128 keys into a
-//               2-stage ring (K K-major, V MN-major as the second operand of P V);
+// One CTA per (batch, query head, block of 128 queries), 11 warps:
+//   warp 0      TMA producer (one thread): the Q block once, then K tiles of 128 keys (K-major)
+//               into a 2-stage ring whose stage is free once S = Q K^T has read it;
+//   warp 10     TMA producer (one thread): V tiles of 128 keys (MN-major, the second operand of
+//               P V) into a 2-stage ring whose stage is free once P V has read it;
 //   warp 1      TMEM owner and MMA issuer (one thread): S_j = Q K_j^T (tcgen05.mma, fp32 in TMEM,
 //               two S buffers so S_{j+1} is computed while the softmax reads S_j), then
 //               O += P_j V_j into an fp32 accumulator that stays in TMEM;
-//   warps 2..5  softmax and epilogue, one query row per thread: the raw logits' running maximum
-//               (the side output, over visible logits only), the online softmax in base 2 with
-//               a lazy rescale (O and the row sum are rescaled only when the row maximum grows by
-//               more than 2^8), P in bf16/fp16 written to shared memory in the 128-byte swizzled
-//               K-major layout the MMA reads, and at the end O / l stored to [B, Sq, Hq, D].
+//   warps 2..9  softmax and epilogue, two warps per TMEM lane quarter (64 keys of a row each):
+//               the raw logits' running maximum (the side output, over visible logits only),
+//               the online softmax in base 2 with a lazy rescale (O and the row sum are rescaled
+//               only when the row maximum grows by more than 2^8), P in bf16/fp16 written to
+//               shared memory in the 128-byte swizzled K-major layout the MMA reads, and at the
+//               end O / l stored to [B, Sq, Hq, D].
 // Visibility: key j of batch b is visible to query i when key_lo[b] <= j < key_hi[b] (padding)
 // and, when causal, j <= i + Sk - Sq. Rows without a visible key are written as zeros.
 // Every wait is bounded; on timeout the kernel records a code in the status word, raises its
@@ -30,11 +33,12 @@ using namespace tc;
 constexpr int AM = 128;          // query rows per CTA (UMMA M)
 constexpr int AN = 128;          // keys per tile: UMMA N of S, the K of P V
 constexpr int ABK = 64;          // 128-byte swizzle row of 16-bit elements
-constexpr int A_THREADS = 320;   // warp 0 TMA, warp 1 MMA, warps 2..9 softmax (two per TMEM lane quarter)
-constexpr int KV_STAGES = 2;
+constexpr int A_THREADS = 352;   // warp 0 TMA of Q and K, warp 1 MMA, warps 2..9 softmax (two streams
+                                 // of four warps, one warp per TMEM lane quarter), warp 10 TMA of V
+constexpr int KV_STAGES = 2;     // one K and one V stage per softmax stream (tile j uses stage j % 2)
 constexpr int SUB_BYTES = 128 * ABK * 2;     // one swizzled block of 128 rows x 64 elements (16 KB)
 constexpr int BOX_BYTES = 64 * ABK * 2;      // one 64 x 64 box of the MN-major V operand (8 KB)
-constexpr uint32_t TMEM_COLS = 512;          // S buffers at 0 and 128, O at 256
+constexpr uint32_t TMEM_COLS = 512;          // S of each stream at 0 and 128, O of each stream from 256
 constexpr float kRescaleLog2 = 8.0f;          // lazy rescale threshold: P stays below 2^8
 
 template <int D>
@@ -42,12 +46,12 @@ struct AttnLayout {
   static constexpr int Q_BYTES = (D / ABK) * SUB_BYTES;
   static constexpr int K_BYTES = (D / ABK) * SUB_BYTES;
   static constexpr int V_BYTES = 2 * (D / ABK) * BOX_BYTES;
-  static constexpr int P_BYTES = 2 * SUB_BYTES;
-  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
-  static constexpr int TILES_BYTES = Q_BYTES + KV_STAGES * STAGE_BYTES + P_BYTES;
-  // tiles, 1 KB of barriers and flags, 3 KB + 96 B of softmax exchange, 1 KB of alignment; at
-  // least 116 KB so that one CTA holds an SM (every CTA allocates all 512 TMEM columns)
-  static constexpr int NEED = TILES_BYTES + 1024 + 6 * AM * 4 + 24 * 4 + 1024;
+  static constexpr int P_BYTES = 2 * SUB_BYTES;   // one 128 x 128 P tile per stream
+  static constexpr int TILES_BYTES = Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES;
+  static constexpr int BAR_BYTES = 256;           // barriers, TMEM address, flags
+  // tiles, barriers and 1 KB of alignment (224.25 KB for D = 128, within the 227 KB a CTA may
+  // use); at least 116 KB so that one CTA holds an SM (every CTA allocates all 512 TMEM columns)
+  static constexpr int NEED = TILES_BYTES + BAR_BYTES + 1024;
   static constexpr int SMEM_BYTES = NEED > 116 * 1024 ? NEED : 116 * 1024;
 };
 
@@ -106,6 +110,18 @@ __device__ __forceinline__ void attn_tiles(const AttnArgs& g, int b, int qb, int
   ntiles = static_cast<int>((end + AN - 1) / AN) - t0;
 }
 
+// Three-input maximum (NaN-propagating) and minimum (sm_100).
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float min3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <int FMT, int D>
 __global__ void __launch_bounds__(A_THREADS, 1)
 attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -115,24 +131,24 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  // K and V have rings of their own: a K stage is free once S_j = Q K_j^T is computed, long before
+  // P_j V_j frees the V stage. Tile j belongs to softmax stream j % 2 and uses K / V stage j % 2,
+  // the stream's S buffer, P buffer and O accumulator.
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + L::Q_BYTES;
-  uint8_t* sP = sKV + KV_STAGES * L::STAGE_BYTES;
+  uint8_t* sK = sQ + L::Q_BYTES;
+  uint8_t* sV = sK + KV_STAGES * L::K_BYTES;
+  uint8_t* sP = sV + KV_STAGES * L::V_BYTES;
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::TILES_BYTES);
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + KV_STAGES;
-  uint64_t* s_full = kv_empty + KV_STAGES;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* o_done = p_full + 1;
-  uint64_t* drain = o_done + 1;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + KV_STAGES;
+  uint64_t* v_full = k_empty + KV_STAGES;
+  uint64_t* v_empty = v_full + KV_STAGES;
+  uint64_t* s_full = v_empty + KV_STAGES;   // [stream]: S of the stream's next tile computed
+  uint64_t* p_full = s_full + 2;            // [stream]: P written (and S read) by the stream's 4 warps
+  uint64_t* o_done = p_full + 2;            // [stream]: P V of the stream's last tile done
+  uint64_t* drain = o_done + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
-  // softmax pair exchange: row maxima [2 tile parities][2 halves][128 rows], then the row sums
-  // [2 halves][128 rows]; each warp's "still running" word [2 parities][2 halves][4 quarters],
-  // then the final one [2 halves][4 quarters]
-  float* red_max = reinterpret_cast<float*>(smem + L::TILES_BYTES + 1024);
-  int* red_ok = reinterpret_cast<int*>(red_max + 6 * AM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b, h, qb;
@@ -144,10 +160,11 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < KV_STAGES; ++s) { mbar_init(kv_full + s, 1); mbar_init(kv_empty + s, 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(s_full + s, 1); mbar_init(s_empty + s, 8); }
-    mbar_init(p_full, 8);
-    mbar_init(o_done, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(k_full + s, 1); mbar_init(k_empty + s, 1);
+      mbar_init(v_full + s, 1); mbar_init(v_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) { mbar_init(s_full + s, 1); mbar_init(p_full + s, 4); mbar_init(o_done + s, 1); }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -162,33 +179,45 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const uint32_t tmem_o = tmem_base + 2 * AN;
+  const uint32_t tmem_o = tmem_base + 2 * AN;   // O of stream s at tmem_o + s * D
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 10) {
+    // ------------------------------------------------------------------ TMA producers
+    // warp 0: Q once, then K_j into K stage j % 2 once S_{j-2} has read it; warp 10: V_j into V
+    // stage j % 2 once P_{j-2} V_{j-2} has read it
     if (lane == 0 && ntiles > 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_v)) : "memory");
-      mbar_arrive_expect_tx(q_full, L::Q_BYTES);
-      for (int kb = 0; kb < NKB; ++kb) tma_load_4d(&map_q, q_full, sQ + kb * SUB_BYTES, kb * ABK, qb * AM, h, b);
+      const bool keys = warp == 0;
+      uint64_t* full = keys ? k_full : v_full;
+      uint64_t* empty = keys ? k_empty : v_empty;
+      const uint32_t stage_bytes = keys ? L::K_BYTES : L::V_BYTES;
+      if (keys) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
+        mbar_arrive_expect_tx(q_full, L::Q_BYTES);
+        for (int kb = 0; kb < NKB; ++kb) tma_load_4d(&map_q, q_full, sQ + kb * SUB_BYTES, kb * ABK, qb * AM, h, b);
+      } else {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_v)) : "memory");
+      }
       bool ok = true;
       uint32_t armed = 0, armed_parity = 0;
       for (int j = 0; j < ntiles; ++j) {
         const int stage = j % KV_STAGES;
         const uint32_t phase = static_cast<uint32_t>((j / KV_STAGES) & 1);
-        if (!mbar_wait(kv_empty + stage, phase ^ 1)) { ok = false; break; }
+        if (!mbar_wait(empty + stage, phase ^ 1)) { ok = false; break; }
         if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
-        uint8_t* sK = sKV + stage * L::STAGE_BYTES;
-        uint8_t* sV = sK + L::K_BYTES;
-        mbar_arrive_expect_tx(kv_full + stage, L::STAGE_BYTES);
+        mbar_arrive_expect_tx(full + stage, stage_bytes);
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
         const int key0 = (t0 + j) * AN;
-        for (int kb = 0; kb < NKB; ++kb) tma_load_4d(&map_k, kv_full + stage, sK + kb * SUB_BYTES, kb * ABK, key0, kvh, b);
-        for (int kc = 0; kc < 2; ++kc)
-          for (int dc = 0; dc < NKB; ++dc)
-            tma_load_4d(&map_v, kv_full + stage, sV + (kc * NKB + dc) * BOX_BYTES, dc * ABK, key0 + kc * 64, kvh, b);
+        if (keys) {
+          uint8_t* dst = sK + stage * L::K_BYTES;
+          for (int kb = 0; kb < NKB; ++kb) tma_load_4d(&map_k, full + stage, dst + kb * SUB_BYTES, kb * ABK, key0, kvh, b);
+        } else {
+          uint8_t* dst = sV + stage * L::V_BYTES;
+          for (int kc = 0; kc < 2; ++kc)
+            for (int dc = 0; dc < NKB; ++dc)
+              tma_load_4d(&map_v, full + stage, dst + (kc * NKB + dc) * BOX_BYTES, dc * ABK, key0 + kc * 64, kvh, b);
+        }
       }
       if (!ok) {
         atomicCAS(g.status, kErrNone, kErrTimeoutProducer);
@@ -196,55 +225,63 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         if (g.valid) atomicExch(g.valid, 0);
       }
       // every load of this CTA must have landed before it may exit (bounded)
-      mbar_wait(q_full, 0);
+      if (keys) mbar_wait(q_full, 0);
       for (int s2 = 0; s2 < KV_STAGES; ++s2)
-        if (armed & (1u << s2)) mbar_wait(kv_full + s2, (armed_parity >> s2) & 1u);
+        if (armed & (1u << s2)) mbar_wait(full + s2, (armed_parity >> s2) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // S_0, S_1 first; then per tile j: once its stream's P_j is written, S_{j+2} (the stream's
+    // next logits, so its softmax can go on) and then O_s += P_j V_j.
     if (lane == 0 && ntiles > 0) {
       constexpr uint32_t idesc_s = make_idesc_fmt(AM, AN, false, false, FMT);
       constexpr uint32_t idesc_pv = make_idesc_fmt(AM, D, false, true, FMT);
-      bool ok = mbar_wait(q_full, 0);
-      auto issue_pv = [&](int t) -> bool {
-        if (!mbar_wait(p_full, static_cast<uint32_t>(t & 1))) return false;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(k_full + s, static_cast<uint32_t>((j >> 1) & 1))) return false;
         if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
         tc_fence_after();
-        const int stage = t % KV_STAGES;
-        const uint32_t sv = smem_u32(sKV + stage * L::STAGE_BYTES + L::K_BYTES);
-        const uint32_t sp = smem_u32(sP);
-#pragma unroll
-        for (int kc = 0; kc < 2; ++kc)
-#pragma unroll
-          for (int k = 0; k < ABK / 16; ++k)
-            umma_f16(tmem_o, make_sdesc(sp + kc * SUB_BYTES + k * 32, 16, 1024),
-                     make_sdesc(sv + kc * NKB * BOX_BYTES + k * (16 * 128), BOX_BYTES, 1024), idesc_pv,
-                     (t > 0 || kc > 0 || k > 0) ? 1u : 0u);
-        umma_commit(kv_empty + stage);  // K_t and V_t read
-        umma_commit(o_done);            // P buffer free, O holds tiles 0..t
-        return true;
-      };
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int stage = j % KV_STAGES;
-        const uint32_t phase = static_cast<uint32_t>((j / KV_STAGES) & 1);
-        const int sb = j & 1;
-        const uint32_t sp = static_cast<uint32_t>((j >> 1) & 1);
-        if (!mbar_wait(kv_full + stage, phase) || !mbar_wait(s_empty + sb, sp ^ 1)) { ok = false; break; }
-        if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
-        tc_fence_after();
         const uint32_t sq_ = smem_u32(sQ);
-        const uint32_t sk_ = smem_u32(sKV + stage * L::STAGE_BYTES);
+        const uint32_t sk_ = smem_u32(sK + s * L::K_BYTES);
 #pragma unroll
         for (int kb = 0; kb < NKB; ++kb)
 #pragma unroll
           for (int k = 0; k < ABK / 16; ++k)
-            umma_f16(tmem_base + sb * AN, make_sdesc(sq_ + kb * SUB_BYTES + k * 32, 16, 1024),
+            umma_f16(tmem_base + s * AN, make_sdesc(sq_ + kb * SUB_BYTES + k * 32, 16, 1024),
                      make_sdesc(sk_ + kb * SUB_BYTES + k * 32, 16, 1024), idesc_s, (kb > 0 || k > 0) ? 1u : 0u);
-        umma_commit(s_full + sb);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        umma_commit(s_full + s);
+        umma_commit(k_empty + s);   // K_j read
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j & 1;
+        const uint32_t use = static_cast<uint32_t>(j >> 1);
+        if (!mbar_wait(v_full + s, use & 1u)) return false;
+        if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t sv = smem_u32(sV + s * L::V_BYTES);
+        const uint32_t sp = smem_u32(sP + s * L::P_BYTES);
+#pragma unroll
+        for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+          for (int k = 0; k < ABK / 16; ++k)
+            umma_f16(tmem_o + s * D, make_sdesc(sp + kc * SUB_BYTES + k * 32, 16, 1024),
+                     make_sdesc(sv + kc * NKB * BOX_BYTES + k * (16 * 128), BOX_BYTES, 1024), idesc_pv,
+                     (use > 0 || kc > 0 || k > 0) ? 1u : 0u);
+        umma_commit(v_empty + s);   // V_j read
+        umma_commit(o_done + s);    // P buffer of the stream free, O_s holds its tiles up to j
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0);
+      if (ok) ok = issue_s(0);
+      if (ok && ntiles > 1) ok = issue_s(1);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        if (!mbar_wait(p_full + (j & 1), static_cast<uint32_t>((j >> 1) & 1))) { ok = false; break; }
+        tc_fence_after();
+        if (j + 2 < ntiles && !issue_s(j + 2)) { ok = false; break; }
+        if (!issue_pv(j)) { ok = false; break; }
       }
-      if (ok) ok = issue_pv(ntiles - 1);
       if (!ok) {
         atomicCAS(g.status, kErrNone, kErrTimeoutMma);
         atomicExch(abort_flag, 1);
@@ -253,172 +290,202 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------------ softmax and epilogue
-    // Two warps per TMEM lane quarter: warp half h takes keys [64 h, 64 h + 64) of every tile,
-    // and columns [h D/2, (h + 1) D/2) of O. The pair exchanges its row maxima once per tile
-    // through shared memory (named barrier 1 + quarter, 64 threads).
+    // ------------------------------------------------------------------ softmax streams and epilogue
+    // Stream s (warps 2..5: s = 0, warps 6..9: s = 1) takes tiles j = s, s + 2, ...: one warp per
+    // TMEM lane quarter, one query row per thread, all 128 keys of the tile. Each stream keeps its
+    // own running maximum, row sum and O accumulator; they are combined once at the end. The two
+    // streams do not wait for each other, so one computes exponentials while the other is in its
+    // maximum pass, and each stream's next S is computed while it works on the current one.
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int stream = (warp - 2) >> 2;
     const int r = 32 * quarter + lane;                 // row of the block == TMEM lane
     const int64_t row = static_cast<int64_t>(qb) * AM + r;
     const bool row_in = row < g.sq;
     const int64_t jmax = g.causal ? row + g.shift : g.sk - 1;  // last key visible by causality
     const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
-    constexpr int HN = AN / 2;         // keys per warp and tile
-    constexpr int HD = D / 2;          // O columns per warp
+    const uint32_t s_cols = tmem_base + lane_addr + stream * AN;
+    const uint32_t o_cols = tmem_o + lane_addr + stream * D;
+    uint8_t* my_p = sP + stream * L::P_BYTES;
+    const int n_mine = (ntiles - stream + 1) / 2;      // tiles of this stream
     float m_run = -INFINITY;    // running maximum of the scaled logits (log2 units) used by P
-    float l_run = 0.0f;         // running sum of this warp's half of P
-    float raw_max = -INFINITY;  // side output: maximum of the visible raw logits q . k
-    bool finite = true;
+    float l_run = 0.0f;         // running sum of P over this stream's tiles
+    float raw_max = -INFINITY;  // side output: maximum of the visible raw logits q . k (NaN-propagating)
+    float raw_min = INFINITY;   // a visible -inf logit shows here
     bool ok = true;
-    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory"); };
-    // The pair leaves the loop together: every failure (an expired wait, an abort) is noted in
-    // `ok` and exchanged at the next per-tile barrier (or the final one), never acted on alone.
-    for (int j = 0; j < ntiles; ++j) {
-      const int sb = j & 1;
-      const uint32_t sp = static_cast<uint32_t>((j >> 1) & 1);
-      bool ready = ok;
-      if (lane == 0 && ready) ready = mbar_wait(s_full + sb, sp);
+    for (int u = 0; u < n_mine; ++u) {
+      const int j = 2 * u + stream;
+      bool ready = true;
+      if (lane == 0) ready = mbar_wait(s_full + stream, static_cast<uint32_t>(u & 1));
       ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
-      ready = ready && !*reinterpret_cast<volatile int*>(abort_flag);
-      red_ok[(j & 1) * 8 + half * 4 + quarter] = ready ? 1 : 0;
-      float s[HN];
-      if (ready) {
-        tc_fence_after();
-        uint32_t v[HN];
-        tmem_ld64(tmem_base + lane_addr + sb * AN + half * HN, v);
-#pragma unroll
-        for (int e = 0; e < HN; ++e) s[e] = __uint_as_float(v[e]);
-        tc_fence_before();
+      if (!ready || *reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      // visible key columns [c_lo, c_hi) of this tile for this row
+      const int64_t key0 = static_cast<int64_t>(t0 + j) * AN;
+      const int64_t end = hi < jmax + 1 ? hi : jmax + 1;
+      int c_lo = 0, c_hi = 0;
+      if (row_in) {
+        const int64_t a0 = lo - key0, a1 = end - key0;
+        c_lo = a0 < 0 ? 0 : (a0 > AN ? AN : static_cast<int>(a0));
+        c_hi = a1 < 0 ? 0 : (a1 > AN ? AN : static_cast<int>(a1));
+        if (c_hi < c_lo) c_hi = c_lo;
       }
-      __syncwarp();
-      if (lane == 0 && ready) mbar_arrive(s_empty + sb);  // S buffer (this half) free for S_{j+2}
-      // visibility of this half tile's keys for this row; partial maxima and the non-finite test
-      const int64_t key0 = static_cast<int64_t>(t0 + j) * AN + half * HN;
-      const bool all_visible = row_in && key0 >= lo && key0 + HN <= hi && key0 + HN - 1 <= jmax;
-      float mp[8];
-      uint32_t badp[8];   // a visible logit with all exponent bits set: +-inf or NaN
+      const bool all_visible = c_lo == 0 && c_hi == AN;
+      // pass 1: the tile's maximum and minimum over the visible logits
+      float mx[4], mn[4];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) { mp[q] = -INFINITY; badp[q] = 0u; }
-      if (all_visible) {
+      for (int q = 0; q < 4; ++q) { mx[q] = -INFINITY; mn[q] = INFINITY; }
 #pragma unroll
-        for (int c = 0; c < HN; ++c) badp[c & 7] |= (__float_as_uint(s[c]) & 0x7fffffffu) >= 0x7f800000u ? 1u : 0u;
-      } else {
-        const int64_t vis_lo = lo - key0, vis_hi_excl = (hi < jmax + 1 ? hi : jmax + 1) - key0;
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t v[64];
+        tmem_ld64(s_cols + ch * 64, v);
+        if (all_visible) {
 #pragma unroll
-        for (int c = 0; c < HN; ++c) {
-          if (!row_in || c < vis_lo || c >= vis_hi_excl) s[c] = -INFINITY;
-          else badp[c & 7] |= (__float_as_uint(s[c]) & 0x7fffffffu) >= 0x7f800000u ? 1u : 0u;
+          for (int c = 0; c < 64; c += 2) {
+            const float x0 = __uint_as_float(v[c]), x1 = __uint_as_float(v[c + 1]);
+            mx[(c >> 1) & 3] = max3_nan(mx[(c >> 1) & 3], x0, x1);
+            mn[(c >> 1) & 3] = min3(mn[(c >> 1) & 3], x0, x1);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const int k0 = ch * 64 + c;
+            const bool v0 = k0 >= c_lo && k0 < c_hi, v1 = k0 + 1 >= c_lo && k0 + 1 < c_hi;
+            const float x0 = __uint_as_float(v[c]), x1 = __uint_as_float(v[c + 1]);
+            mx[(c >> 1) & 3] = max3_nan(mx[(c >> 1) & 3], v0 ? x0 : -INFINITY, v1 ? x1 : -INFINITY);
+            mn[(c >> 1) & 3] = min3(mn[(c >> 1) & 3], v0 ? x0 : INFINITY, v1 ? x1 : INFINITY);
+          }
         }
       }
-#pragma unroll
-      for (int c = 0; c < HN; ++c) mp[c & 7] = fmaxf(mp[c & 7], s[c]);
-      const float mine = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-      finite = finite && (badp[0] | badp[1] | badp[2] | badp[3] | badp[4] | badp[5] | badp[6] | badp[7]) == 0u;
-      raw_max = fmaxf(raw_max, mine);
-      // exchange the half-row maxima (double-buffered by tile parity)
-      red_max[((j & 1) * 2 + half) * AM + r] = mine;
-      pair_sync();
-      const float other = red_max[((j & 1) * 2 + (half ^ 1)) * AM + r];
-      const bool pair_ok = red_ok[(j & 1) * 8 + (half ^ 1) * 4 + quarter] != 0;
-      if (!ready || !pair_ok) { ok = false; break; }
-      const float mt = fmaxf(mine, other);
-      // lazy online softmax in base 2 (both halves reach the same m_run and alpha)
+      const float mt = max3_nan(max3_nan(mx[0], mx[1], mx[2]), mx[3], -INFINITY);
+      raw_max = max3_nan(raw_max, mt, -INFINITY);
+      raw_min = min3(min3(raw_min, mn[0], mn[1]), mn[2], mn[3]);
+      // lazy online softmax in base 2
       const float mt2 = mt * g.scale_log2;
       float alpha = 1.0f;
       bool rescale = false;
       if (mt2 > m_run + kRescaleLog2) {
         alpha = m_run == -INFINITY ? 0.0f : fast_exp2(m_run - mt2);
-        rescale = j > 0;
+        rescale = u > 0;
         m_run = mt2;
       }
-      float lp[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) lp[q] = 0.0f;
-      uint32_t packed[HN / 2];
-      if (m_run == -INFINITY) {
-#pragma unroll
-        for (int c = 0; c < HN / 2; ++c) packed[c] = 0u;
-      } else {
-#pragma unroll
-        for (int c = 0; c < HN; c += 2) {
-          const float p0 = fast_exp2(fmaf(s[c], g.scale_log2, -m_run));
-          const float p1 = fast_exp2(fmaf(s[c + 1], g.scale_log2, -m_run));
-          lp[(c >> 1) & 7] += p0 + p1;
-          if (FMT == 1) packed[c / 2] = pack_bf16(p0, p1);
-          else packed[c / 2] = pack_half(p0, p1);
-        }
-      }
-      const float lsum = ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
-      l_run = l_run * alpha + lsum;
-      // P V of the previous tile must be done: the P buffer is reused and O may be rescaled
-      if (j > 0) {
+      // P V of this stream's previous tile must be done: its P buffer is reused and O may be rescaled
+      if (u > 0) {
         bool done = true;
-        if (lane == 0) done = mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1));
+        if (lane == 0) done = mbar_wait(o_done + stream, static_cast<uint32_t>((u - 1) & 1));
         done = __shfl_sync(0xffffffffu, done ? 1 : 0, 0) != 0;
-        if (!done) { ok = false; continue; }   // the next barrier ends the pair's loop
+        if (!done) { ok = false; break; }
         tc_fence_after();
       }
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
           uint32_t v[32];
-          tmem_ld32(tmem_o + lane_addr + half * HD + c * 32, v);
+          tmem_ld32(o_cols + c * 32, v);
           if (rescale) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
           }
-          tmem_st32(tmem_o + lane_addr + half * HD + c * 32, v);
+          tmem_st32(o_cols + c * 32, v);
         }
       }
-      // this half of the P row into K block `half` of the swizzled K-major layout: chunk c16 of
-      // 8 keys sits at row * 128 + ((c16 ^ (row & 7)) * 16)
+      // pass 2: P = 2^(s * scale_log2 - m_run), its row sum, and P in the 128-byte swizzled K-major
+      // layout (chunk c16 of 8 keys of K block ch sits at row * 128 + ((c16 ^ (row & 7)) * 16))
+      const float nm = -m_run;
+      float lsum[8];
 #pragma unroll
-      for (int c16 = 0; c16 < HN / 8; ++c16) {
-        uint8_t* dst = sP + half * SUB_BYTES + r * 128 + ((c16 ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) =
-            make_uint4(packed[4 * c16], packed[4 * c16 + 1], packed[4 * c16 + 2], packed[4 * c16 + 3]);
+      for (int q = 0; q < 8; ++q) lsum[q] = 0.0f;
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t v[64];
+        tmem_ld64(s_cols + ch * 64, v);
+        uint32_t packed[32];
+        if (m_run == -INFINITY) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) packed[c] = 0u;
+        } else if (all_visible) {
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(v[c]), g.scale_log2, nm));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(v[c + 1]), g.scale_log2, nm));
+            lsum[(c >> 1) & 3] += p0;
+            lsum[((c >> 1) & 3) + 4] += p1;
+            packed[c >> 1] = FMT == 1 ? pack_bf16(p0, p1) : pack_half(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const int k0 = ch * 64 + c;
+            const float x0 = (k0 >= c_lo && k0 < c_hi) ? __uint_as_float(v[c]) : -INFINITY;
+            const float x1 = (k0 + 1 >= c_lo && k0 + 1 < c_hi) ? __uint_as_float(v[c + 1]) : -INFINITY;
+            const float p0 = fast_exp2(fmaf(x0, g.scale_log2, nm));
+            const float p1 = fast_exp2(fmaf(x1, g.scale_log2, nm));
+            lsum[(c >> 1) & 3] += p0;
+            lsum[((c >> 1) & 3) + 4] += p1;
+            packed[c >> 1] = FMT == 1 ? pack_bf16(p0, p1) : pack_half(p0, p1);
+          }
+        }
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16) {
+          uint8_t* dst = my_p + ch * SUB_BYTES + r * 128 + ((c16 ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) =
+              make_uint4(packed[4 * c16], packed[4 * c16 + 1], packed[4 * c16 + 2], packed[4 * c16 + 3]);
+        }
       }
+      l_run = l_run * alpha + (((lsum[0] + lsum[1]) + (lsum[2] + lsum[3])) + ((lsum[4] + lsum[5]) + (lsum[6] + lsum[7])));
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full + stream);
     }
-    // epilogue: O / l of this row, this warp's half of the columns
-    if (ok && ntiles > 0) {
+    // this stream's last P V must be done before O_s is read and its P buffer is reused
+    if (ok && n_mine > 0) {
       bool done = true;
-      if (lane == 0) done = mbar_wait(o_done, static_cast<uint32_t>((ntiles - 1) & 1));
+      if (lane == 0) done = mbar_wait(o_done + stream, static_cast<uint32_t>((n_mine - 1) & 1));
       done = __shfl_sync(0xffffffffu, done ? 1 : 0, 0) != 0;
       if (!done) ok = false;
       tc_fence_after();
     }
-    // the row sum is the two halves' sums (both warps of the pair reach this barrier together:
-    // a failed wait ends both loops at the same tile)
-    red_max[(4 + half) * AM + r] = l_run;
-    red_ok[16 + half * 4 + quarter] = ok;
-    pair_sync();
-    const float l_total = l_run + red_max[(4 + (half ^ 1)) * AM + r];
-    ok = ok && red_ok[16 + (half ^ 1) * 4 + quarter] != 0;
-    if (ok) {
+    // combine the two streams of each row: the warps of a TMEM lane quarter (one per stream)
+    // exchange (m, l, ok) through their P buffers and each writes half of the row's columns of
+    // O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m))
+    float* xch = reinterpret_cast<float*>(my_p);
+    xch[r] = m_run;
+    xch[AM + r] = l_run;
+    reinterpret_cast<int*>(xch)[2 * AM + r] = ok ? 1 : 0;
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+    const float* other = reinterpret_cast<const float*>(sP + (stream ^ 1) * L::P_BYTES);
+    const float m_o = other[r], l_o = other[AM + r];
+    ok = ok && reinterpret_cast<const int*>(other)[2 * AM + r] != 0;
+    const int n_other = (ntiles - (stream ^ 1) + 1) / 2;
+    if (__all_sync(0xffffffffu, ok)) {
+      const float m_all = fmaxf(m_run, m_o);
+      const float a_me = m_run == -INFINITY ? 0.0f : fast_exp2(m_run - m_all);
+      const float a_ot = m_o == -INFINITY ? 0.0f : fast_exp2(m_o - m_all);
+      const float l_total = l_run * a_me + l_o * a_ot;
       const float inv = l_total > 0.0f ? 1.0f / l_total : 0.0f;
+      const float w0 = (stream == 0 ? a_me : a_ot) * inv;   // weight of O_0
+      const float w1 = (stream == 0 ? a_ot : a_me) * inv;   // weight of O_1
+      const bool have0 = (stream == 0 ? n_mine : n_other) > 0;
+      const bool have1 = (stream == 0 ? n_other : n_mine) > 0;
+      constexpr int HD = D / 2;   // output columns per warp
       uint16_t* orow = reinterpret_cast<uint16_t*>(g.out) + static_cast<int64_t>(b) * g.o_sb +
-                       static_cast<int64_t>(h) * g.o_sh + row * g.o_ss + half * HD;
+                       static_cast<int64_t>(h) * g.o_sh + row * g.o_ss + stream * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v[32];
-        if (ntiles > 0) tmem_ld32(tmem_o + lane_addr + half * HD + c * 32, v);
-        else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = 0u;
-        }
+        uint32_t v0[32], v1[32];
+        const uint32_t col = lane_addr + stream * HD + c * 32;
+        if (have0) tmem_ld32(tmem_o + col, v0);
+        if (have1) tmem_ld32(tmem_o + D + col, v1);
         if (row_in) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float o0 = __uint_as_float(v[8 * q + 2 * e]) * inv;
-              const float o1 = __uint_as_float(v[8 * q + 2 * e + 1]) * inv;
+              const int i0 = 8 * q + 2 * e;
+              float o0 = 0.0f, o1 = 0.0f;
+              if (have0) { o0 = __uint_as_float(v0[i0]) * w0; o1 = __uint_as_float(v0[i0 + 1]) * w0; }
+              if (have1) { o0 = fmaf(__uint_as_float(v1[i0]), w1, o0); o1 = fmaf(__uint_as_float(v1[i0 + 1]), w1, o1); }
               w[e] = FMT == 1 ? pack_bf16(o0, o1) : pack_half(o0, o1);
             }
             *reinterpret_cast<uint4*>(orow + c * 32 + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -428,9 +495,14 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       if (g.enc != nullptr) {
         float m = raw_max;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0 && m > -INFINITY) atomicMax(g.enc + h, encode_max(m));
-        if (!finite) atomicExch(g.valid, 0);
+        for (int o = 16; o > 0; o >>= 1) m = max3_nan(m, __shfl_xor_sync(0xffffffffu, m, o), -INFINITY);
+        float mnv = raw_min;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mnv = fminf(mnv, __shfl_xor_sync(0xffffffffu, mnv, o));
+        if (lane == 0) {
+          if (m != m || m == INFINITY || mnv == -INFINITY) atomicExch(g.valid, 0);
+          else if (m > -INFINITY) atomicMax(g.enc + h, encode_max(m));
+        }
       }
     } else if (lane == 0) {
       atomicCAS(g.status, kErrNone, kErrTimeoutEpilogue);

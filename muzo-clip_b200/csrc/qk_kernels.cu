@@ -13,7 +13,8 @@ namespace muzo {
 
 int qk_max_tensor_cores(const void* q, const void* k, int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t sq,
                         int64_t sk, int64_t d, int64_t qsb, int64_t qsh, int64_t qss, int64_t ksb, int64_t ksh,
-                        int64_t kss, int causal, int* enc, int32_t* valid, cudaStream_t stream);
+                        int64_t kss, int causal, const int32_t* key_lo, const int32_t* key_hi, int* enc,
+                        int32_t* valid, cudaStream_t stream);
 
 namespace {
 
@@ -48,8 +49,8 @@ template <int DTYPE>
 __global__ void __launch_bounds__(256)
 qk_max_simt_kernel(const char* __restrict__ q, const char* __restrict__ k, int64_t hq, int64_t hkv,
                    int64_t sq, int64_t sk, int64_t d, int64_t qsb, int64_t qsh, int64_t qss,
-                   int64_t ksb, int64_t ksh, int64_t kss, int causal, int* __restrict__ enc,
-                   int32_t* __restrict__ valid) {
+                   int64_t ksb, int64_t ksh, int64_t kss, int causal, const int32_t* __restrict__ key_lo,
+                   const int32_t* __restrict__ key_hi, int* __restrict__ enc, int32_t* __restrict__ valid) {
   __shared__ float qs[DCHUNK][QT + 1];
   __shared__ float ks[DCHUNK][KT + 1];
   const int64_t qtiles = (sq + QT - 1) / QT;
@@ -64,11 +65,15 @@ qk_max_simt_kernel(const char* __restrict__ q, const char* __restrict__ k, int64
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int64_t i0 = qt * QT;
   const int64_t shift = sk - sq;  // causal: key j visible to query i when j <= i + shift
-  int64_t kend = sk;
-  if (causal) kend = min(sk, i0 + QT + shift);
+  int64_t kbegin = 0, kend = sk;   // visible keys of this batch row: [kbegin, kend)
+  if (key_lo != nullptr) {
+    kbegin = max(static_cast<int64_t>(key_lo[b]), static_cast<int64_t>(0));
+    kend = min(static_cast<int64_t>(key_hi[b]), sk);
+  }
+  const int64_t kstop = causal ? min(kend, i0 + QT + shift) : kend;
   float best = -INFINITY;
   bool finite = true;
-  for (int64_t j0 = 0; j0 < kend; j0 += KT) {
+  for (int64_t j0 = kbegin - kbegin % KT; j0 < kstop; j0 += KT) {
     float acc[4][4] = {};
     for (int64_t c0 = 0; c0 < d; c0 += DCHUNK) {
       for (int e = threadIdx.x; e < DCHUNK * QT; e += 256) {
@@ -97,7 +102,7 @@ qk_max_simt_kernel(const char* __restrict__ q, const char* __restrict__ k, int64
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         const int64_t j = j0 + tx * 4 + v;
-        if (i < sq && j < sk && (!causal || j <= i + shift)) {
+        if (i < sq && j >= kbegin && j < kend && (!causal || j <= i + shift)) {
           const float x = acc[u][v];
           finite = finite && isfinite(x);
           best = fmaxf(best, x);
@@ -178,8 +183,19 @@ int muzo_qk_max(const void* q, const void* k, int dtype, int64_t batch, int64_t 
                 int64_t seq_q, int64_t seq_k, int64_t head_dim, int64_t q_stride_b, int64_t q_stride_h,
                 int64_t q_stride_s, int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
                 int causal, float scale, float* smax, int32_t* d_valid, void* stream) {
+  return muzo_qk_max_ranges(q, k, dtype, batch, hq, hkv, seq_q, seq_k, head_dim, q_stride_b, q_stride_h, q_stride_s,
+                            k_stride_b, k_stride_h, k_stride_s, causal, nullptr, nullptr, scale, smax, d_valid,
+                            stream);
+}
+
+int muzo_qk_max_ranges(const void* q, const void* k, int dtype, int64_t batch, int64_t hq, int64_t hkv,
+                       int64_t seq_q, int64_t seq_k, int64_t head_dim, int64_t q_stride_b, int64_t q_stride_h,
+                       int64_t q_stride_s, int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_s,
+                       int causal, const int32_t* d_key_lo, const int32_t* d_key_hi, float scale, float* smax,
+                       int32_t* d_valid, void* stream) {
   if (q == nullptr || k == nullptr || smax == nullptr || d_valid == nullptr || batch < 0 || hq <= 0 ||
-      hkv <= 0 || hq % hkv != 0 || seq_q < 0 || seq_k < 0 || head_dim <= 0)
+      hkv <= 0 || hq % hkv != 0 || seq_q < 0 || seq_k < 0 || head_dim <= 0 ||
+      (d_key_lo == nullptr) != (d_key_hi == nullptr))
     return MUZO_ERR_ARG;
   if (dtype != MUZO_BF16 && dtype != MUZO_F16 && dtype != MUZO_F32) return MUZO_ERR_DTYPE;  // before any launch
   if (hq > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;
@@ -198,7 +214,8 @@ int muzo_qk_max(const void* q, const void* k, int dtype, int64_t batch, int64_t 
                            seq_k <= 0x7fffffffLL && qk_tensor_cores_enabled();
   if (tensor_path && units > 0 && seq_k > 0) {
     const int st = qk_max_tensor_cores(q, k, dtype, batch, hq, hkv, seq_q, seq_k, head_dim, q_stride_b, q_stride_h,
-                                       q_stride_s, k_stride_b, k_stride_h, k_stride_s, causal, enc, d_valid, s);
+                                       q_stride_s, k_stride_b, k_stride_h, k_stride_s, causal, d_key_lo, d_key_hi, enc,
+                                       d_valid, s);
     if (st != MUZO_OK) return st;
   } else if (units > 0 && seq_k > 0) {
     if (units > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;
@@ -209,17 +226,17 @@ int muzo_qk_max(const void* q, const void* k, int dtype, int64_t batch, int64_t 
       case MUZO_BF16:
         qk_max_simt_kernel<MUZO_BF16><<<grid, 256, 0, s>>>(qp, kp, hq, hkv, seq_q, seq_k, head_dim, q_stride_b,
                                                            q_stride_h, q_stride_s, k_stride_b, k_stride_h,
-                                                           k_stride_s, causal, enc, d_valid);
+                                                           k_stride_s, causal, d_key_lo, d_key_hi, enc, d_valid);
         break;
       case MUZO_F16:
         qk_max_simt_kernel<MUZO_F16><<<grid, 256, 0, s>>>(qp, kp, hq, hkv, seq_q, seq_k, head_dim, q_stride_b,
                                                           q_stride_h, q_stride_s, k_stride_b, k_stride_h,
-                                                          k_stride_s, causal, enc, d_valid);
+                                                          k_stride_s, causal, d_key_lo, d_key_hi, enc, d_valid);
         break;
       case MUZO_F32:
         qk_max_simt_kernel<MUZO_F32><<<grid, 256, 0, s>>>(qp, kp, hq, hkv, seq_q, seq_k, head_dim, q_stride_b,
                                                           q_stride_h, q_stride_s, k_stride_b, k_stride_h,
-                                                          k_stride_s, causal, enc, d_valid);
+                                                          k_stride_s, causal, d_key_lo, d_key_hi, enc, d_valid);
         break;
       default:
         return MUZO_ERR_DTYPE;

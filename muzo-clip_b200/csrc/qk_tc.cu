@@ -36,6 +36,8 @@ struct QkArgs {
   int64_t sq, sk, shift;
   int hq, hkv, group, nqt, causal, num_kb;
   int64_t tiles_per_bh, num_tiles;
+  const int32_t* key_lo;   // per batch: visible keys [key_lo[b], key_hi[b]); NULL: all keys
+  const int32_t* key_hi;
   int* enc;
   int32_t* valid;
   int32_t* status;
@@ -44,6 +46,18 @@ struct QkArgs {
 __device__ __forceinline__ int encode_max(float f) {
   const int b = __float_as_int(f);
   return b >= 0 ? b : b ^ 0x7fffffff;
+}
+
+// The visible key range [lo, hi) of batch row b, clamped to [0, sk].
+__device__ __forceinline__ void key_range(const int32_t* key_lo, const int32_t* key_hi, int64_t b, int64_t sk,
+                                          int64_t& lo, int64_t& hi) {
+  lo = 0;
+  hi = sk;
+  if (key_lo != nullptr) {
+    const int64_t l = __ldg(key_lo + b), h = __ldg(key_hi + b);
+    lo = l > 0 ? l : 0;
+    hi = h < sk ? h : sk;
+  }
 }
 
 __device__ __forceinline__ int kv_tiles(const QkArgs& g, int qt) {
@@ -181,7 +195,10 @@ qk_max_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
       if (!ready || *reinterpret_cast<volatile int*>(abort_flag)) { ok = ready; break; }
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(qt) * QM + lane_base + lane;
-      const int64_t jlim_causal = row + g.shift;  // last visible key of this row
+      int64_t jmin, jend;
+      key_range(g.key_lo, g.key_hi, bh / g.hq, g.sk, jmin, jend);
+      int64_t jmax = jend - 1;                     // last visible key of this row
+      if (g.causal && row + g.shift < jmax) jmax = row + g.shift;
       float best = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < QN / 32; ++c) {
@@ -189,7 +206,7 @@ qk_max_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
         tmem_ld32(tmem_base + (static_cast<uint32_t>(lane_base) << 16) + acc * QN + c * 32, r);
         const int64_t j0 = static_cast<int64_t>(kv) * QN + c * 32;
         const bool row_ok = row < g.sq;
-        const bool all_ok = row_ok && j0 + 31 < g.sk && (!g.causal || j0 + 31 <= jlim_causal);
+        const bool all_ok = row_ok && j0 >= jmin && j0 + 31 <= jmax;
         if (all_ok) {
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
@@ -201,7 +218,7 @@ qk_max_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int64_t j = j0 + e;
-            if (j < g.sk && (!g.causal || j <= jlim_causal)) {
+            if (j >= jmin && j <= jmax) {
               const float x = __uint_as_float(r[e]);
               finite = finite && isfinite(x);
               best = fmaxf(best, x);
@@ -267,6 +284,8 @@ struct QkPairArgs {
   int hq, group, nqb, causal, num_kb;
   int k_stages;            // key stages in the shared memory the query buffers leave
   int64_t tiles_per_bh, num_tiles;
+  const int32_t* key_lo;   // per batch: visible keys [key_lo[b], key_hi[b]); NULL: all keys
+  const int32_t* key_hi;
   int* enc;
   int32_t* valid;
   int32_t* status;
@@ -485,6 +504,7 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
       low = INFINITY;
     };
     int64_t local = 0;
+    int64_t key_begin = 0, key_end = g.sk;
     PairTileCursor cur;
     cur.start(g, t_begin);
     for (int64_t t = t_begin; t < t_end; ++t, ++local, cur.advance(g)) {
@@ -493,6 +513,7 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
       if (bh != cur_bh) {
         if (cur_bh >= 0) flush(cur_bh);
         cur_bh = bh;
+        key_range(g.key_lo, g.key_hi, bh / g.hq, g.sk, key_begin, key_end);
       }
       const int acc = static_cast<int>(local & 1);
       bool ready = true;
@@ -502,8 +523,8 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(qb) * 2 * PQ_ROWS + static_cast<int64_t>(rank) * PQ_ROWS +
                           32 * quarter + lane;
-      const int64_t jlim = g.causal ? row + g.shift : g.sk - 1;   // last visible key of this row
-      const int64_t jmax = jlim < g.sk - 1 ? jlim : g.sk - 1;
+      int64_t jmax = key_end - 1;                  // last visible key of this row
+      if (g.causal && row + g.shift < jmax) jmax = row + g.shift;
       const int64_t j0 = static_cast<int64_t>(kv) * 2 * PK_ROWS + colh * 128;
       uint32_t r[128];
       tmem_ld128(tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) + acc * QN + colh * 128, r);
@@ -511,7 +532,7 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
-      if (row < g.sq && j0 + 127 <= jmax) {
+      if (row < g.sq && j0 >= key_begin && j0 + 127 <= jmax) {
         // eight independent max / min chains instead of one 128-long dependency chain
         float m[8], n[8];
 #pragma unroll
@@ -524,10 +545,10 @@ qk_max_pair_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_const
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) { best = max_nan(best, m[e]); low = fminf(low, n[e]); }
-      } else if (row < g.sq && j0 <= jmax) {
+      } else if (row < g.sq && j0 <= jmax && j0 + 127 >= key_begin) {
 #pragma unroll
         for (int e = 0; e < 128; ++e) {
-          if (j0 + e <= jmax) {
+          if (j0 + e <= jmax && j0 + e >= key_begin) {
             const float x = __uint_as_float(r[e]);
             best = max_nan(best, x);
             low = fminf(low, x);
@@ -605,7 +626,8 @@ __device__ int32_t g_qk_status;
 // CTA-pair launch (head dim up to 256): contiguous tile ranges over min(tiles, co-resident pairs).
 int qk_max_pair(const void* q, const void* k, int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t sq,
                 int64_t sk, int64_t d, int64_t qsb, int64_t qsh, int64_t qss, int64_t ksb, int64_t ksh, int64_t kss,
-                int causal, int* enc, int32_t* valid, cudaStream_t stream) {
+                int causal, const int32_t* key_lo, const int32_t* key_hi, int* enc, int32_t* valid,
+                cudaStream_t stream) {
   CUtensorMap mq, mk;
   int st = encode_qk_map(&mq, q, dtype, d, sq, hq, batch, qss, qsh, qsb, PQ_ROWS);
   if (st != MUZO_OK) return st;
@@ -631,6 +653,8 @@ int qk_max_pair(const void* q, const void* k, int dtype, int64_t batch, int64_t 
   }
   g.tiles_per_bh = per;
   g.num_tiles = per * batch * hq;
+  g.key_lo = key_lo;
+  g.key_hi = key_hi;
   g.enc = enc;
   g.valid = valid;
   void* p = nullptr;
@@ -664,11 +688,12 @@ int qk_max_pair(const void* q, const void* k, int dtype, int64_t batch, int64_t 
 
 int qk_max_tensor_cores(const void* q, const void* k, int dtype, int64_t batch, int64_t hq, int64_t hkv, int64_t sq,
                         int64_t sk, int64_t d, int64_t qsb, int64_t qsh, int64_t qss, int64_t ksb, int64_t ksh,
-                        int64_t kss, int causal, int* enc, int32_t* valid, cudaStream_t stream) {
+                        int64_t kss, int causal, const int32_t* key_lo, const int32_t* key_hi, int* enc,
+                        int32_t* valid, cudaStream_t stream) {
   const char* pv = std::getenv("MUZO_QK_PAIR");
   if (d <= PQ_MAX_KB * QBK && !(pv != nullptr && pv[0] == '0'))
-    return qk_max_pair(q, k, dtype, batch, hq, hkv, sq, sk, d, qsb, qsh, qss, ksb, ksh, kss, causal, enc, valid,
-                       stream);
+    return qk_max_pair(q, k, dtype, batch, hq, hkv, sq, sk, d, qsb, qsh, qss, ksb, ksh, kss, causal, key_lo, key_hi,
+                       enc, valid, stream);
   CUtensorMap mq, mk;
   int st = encode_qk_map(&mq, q, dtype, d, sq, hq, batch, qss, qsh, qsb, QM);
   if (st != MUZO_OK) return st;
@@ -692,6 +717,8 @@ int qk_max_tensor_cores(const void* q, const void* k, int dtype, int64_t batch, 
   }
   g.tiles_per_bh = per;
   g.num_tiles = per * batch * hq;
+  g.key_lo = key_lo;
+  g.key_hi = key_hi;
   g.enc = enc;
   g.valid = valid;
   void* p = nullptr;

@@ -102,6 +102,11 @@ _SIGNATURES = {
          _vp, _vp],
         _i32,
     ),
+    "muzo_qk_max_ranges": (
+        [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _vp,
+         _f32, _vp, _vp, _vp],
+        _i32,
+    ),
     "muzo_logits_head_max": ([_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp], _i32),
     "muzo_max_merge": ([_vp, _vp, _vp, _i64, _vp], _i32),
     "muzo_ns_normalize_noalloc": ([_vp, _vp, _vp, _i32, _i32, _vp, _vp], _i32),
@@ -133,7 +138,7 @@ KERNELS_PER_CALL = {
     "muzo_perturb_kept_noise": 1, "muzo_rebuild_segments": 1, "muzo_rebuild_segments_kept": 1,
     "muzo_ns_prepare": 1, "muzo_rebuild_segments_history": 1, "muzo_rebuild_kept_linear": 1,
     "muzo_ns_normalize": 1, "muzo_ns_gemm": 1, "muzo_update_sumsq": 1, "muzo_apply_update": 1,
-    "muzo_qk_scale_rows": 1, "muzo_qk_max": 3, "muzo_logits_head_max": 3, "muzo_max_merge": 1,
+    "muzo_qk_scale_rows": 1, "muzo_qk_max": 3, "muzo_qk_max_ranges": 3, "muzo_logits_head_max": 3, "muzo_max_merge": 1,
     "muzo_ns_normalize_noalloc": 3, "muzo_attention_max": 3, "muzo_ipc_export": 0, "muzo_ipc_import": 0, "muzo_ipc_close": 0,
     "muzo_push_blocks": 0,
 }

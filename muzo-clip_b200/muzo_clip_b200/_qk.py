@@ -48,16 +48,24 @@ def logits_head_max(logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: bool,
                 attention_mask: torch.Tensor | None) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-head max of the eager pre-softmax logits of one attention call, from Q [B, Hq, Sq, D]
-    and K [B, Hkv, Sk, D] (any strides with D contiguous)."""
+    and K [B, Hkv, Sk, D] (any strides with D contiguous). A padding mask (per batch row a
+    contiguous range of visible keys, with or without causality) runs on the same kernels with
+    per-batch key ranges; any other mask reduces explicit logits."""
     _check_cuda(query)
-    if attention_mask is not None and not _is_plain_causal(attention_mask, query.shape[2], key.shape[2]):
-        # a mask that is not the plain causal mask (padding): reduce explicit logits
+    key_lo = key_hi = None
+    ranges = None
+    if attention_mask is not None:
+        ranges = mask_key_ranges(attention_mask, query.shape[0], query.shape[2], key.shape[2])
+    if attention_mask is not None and ranges is None:
+        # a mask that is not a padding mask (e.g. block-diagonal or per-head): reduce explicit logits
         group = query.shape[1] // key.shape[1]
         kr = key.repeat_interleave(group, dim=1)
         if attention_mask.dtype == torch.bool:
             attention_mask = eager_additive_mask(attention_mask, causal, query.dtype)
         logits = torch.matmul(query, kr.transpose(2, 3)) * scaling + attention_mask
         return logits_head_max(logits)
+    if ranges is not None:
+        causal, key_lo, key_hi = ranges
     q, k = query, key
     if q.stride(-1) != 1:
         q = q.contiguous()
@@ -67,10 +75,10 @@ def qk_head_max(query: torch.Tensor, key: torch.Tensor, scaling: float, causal: 
     hkv, sk = int(k.shape[1]), int(k.shape[2])
     out = torch.empty(hq, dtype=torch.float32, device=q.device)
     valid = torch.empty(1, dtype=torch.int32, device=q.device)
-    _lib.launch("muzo_qk_max", q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), b, hq, hkv, sq, sk, d,
-                             q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
-                             1 if causal else 0, float(scaling), out.data_ptr(), valid.data_ptr(),
-                             _lib.stream_ptr(q.device))
+    _lib.launch("muzo_qk_max_ranges", q.data_ptr(), k.data_ptr(), _lib.dtype_code(q.dtype), b, hq, hkv, sq, sk, d,
+                q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), 1 if causal else 0,
+                key_lo.data_ptr() if key_lo is not None else None, key_hi.data_ptr() if key_hi is not None else None,
+                float(scaling), out.data_ptr(), valid.data_ptr(), _lib.stream_ptr(q.device))
     return out, valid
 
 
@@ -87,42 +95,78 @@ def eager_additive_mask(keep: torch.Tensor, causal: bool, dtype: torch.dtype) ->
     return torch.zeros(keep.shape, dtype=dtype, device=keep.device).masked_fill(~keep, torch.finfo(dtype).min)
 
 
-# mask object id -> (weak reference, (sq, sk, version), result): transformers builds one mask per
-# forward and hands the same tensor to every layer, so the test (two host syncs) runs once per
-# forward instead of once per layer
-_CAUSAL_CACHE: dict[int, tuple] = {}
+# mask object id -> (weak reference, (batch, sq, sk, version), result): transformers builds one
+# mask per forward and hands the same tensor to every layer, so the classification (one host
+# sync) runs once per forward instead of once per layer
+_RANGES_CACHE: dict[int, tuple] = {}
 
 
-def _is_plain_causal(mask: torch.Tensor, sq: int, sk: int) -> bool:
-    """True when a [B|1, 1|H, Sq, Sk] mask is the plain causal mask for every batch row: an
-    additive mask 0 on and below the (end-aligned) diagonal and a large negative value above
-    it, or a boolean mask True exactly on and below it. Cached per mask tensor and version."""
+def mask_key_ranges(mask: torch.Tensor, batch: int, sq: int, sk: int):
+    """Classify a [B|1, 1, Sq, Sk] attention mask (boolean, True = attend, or additive: 0 or at
+    most half the dtype's minimum). Returns (causal, key_lo, key_hi) when every batch row b
+    attends exactly to the keys [lo_b, hi_b) — and, when causal, only to those at or below the
+    end-aligned diagonal — with key_lo / key_hi int32 device tensors [batch], or both None when
+    every row sees all keys (no padding); None for any other mask. A query row that sees no key
+    under the causal pattern may attend everywhere in a boolean mask (transformers lets such
+    padding rows attend so that SDPA returns no NaN): eager attention masks it, and so does this
+    classification. Cached per mask tensor and version."""
     try:
-        key = (int(sq), int(sk), mask._version)
+        key = (int(batch), int(sq), int(sk), mask._version)
     except RuntimeError:  # inference tensors track no version: no caching
-        return _plain_causal_uncached(mask, sq, sk)
-    entry = _CAUSAL_CACHE.get(id(mask))
+        return _key_ranges_uncached(mask, batch, sq, sk)
+    entry = _RANGES_CACHE.get(id(mask))
     if entry is not None and entry[0]() is mask and entry[1] == key:
         return entry[2]
-    result = _plain_causal_uncached(mask, sq, sk)
-    if len(_CAUSAL_CACHE) >= 64:
-        _CAUSAL_CACHE.clear()
-    _CAUSAL_CACHE[id(mask)] = (weakref.ref(mask), key, result)
+    result = _key_ranges_uncached(mask, batch, sq, sk)
+    if len(_RANGES_CACHE) >= 64:
+        _RANGES_CACHE.clear()
+    _RANGES_CACHE[id(mask)] = (weakref.ref(mask), key, result)
     return result
 
 
-def _plain_causal_uncached(mask: torch.Tensor, sq: int, sk: int) -> bool:
-    if mask.ndim != 4 or mask.shape[-2] != sq or mask.shape[-1] != sk:
-        return False
-    i = torch.arange(sq, device=mask.device)[:, None] + (sk - sq)
-    j = torch.arange(sk, device=mask.device)[None, :]
-    upper = j > i
+def _key_ranges_uncached(mask: torch.Tensor, batch: int, sq: int, sk: int):
+    if mask.ndim != 4 or mask.shape[1] != 1 or mask.shape[-2] != sq or mask.shape[-1] != sk:
+        return None
+    if mask.shape[0] not in (1, batch) or sq == 0 or sk == 0:
+        return None
+    dev = mask.device
     if mask.dtype == torch.bool:
-        return bool((mask == ~upper).all())
-    m = mask.float()
-    lower_ok = bool((m[..., ~upper] == 0).all())
-    upper_ok = bool((m[..., upper] <= torch.finfo(torch.bfloat16).min / 2).all()) if upper.any() else True
-    return lower_ok and upper_ok
+        keep = mask[:, 0]
+        binary = torch.ones((), dtype=torch.bool, device=dev)
+    elif mask.is_floating_point():
+        m = mask[:, 0]
+        keep = m == 0
+        binary = (keep | (m <= torch.finfo(m.dtype).min / 2)).all()
+    else:
+        return None
+    j = torch.arange(sk, device=dev)
+    # the last query row sees the whole range under both patterns (never a padding row without
+    # keys, which a boolean mask may have let attend everywhere)
+    seen = keep[:, -1, :]                                             # [B', Sk]
+    lo = torch.where(seen, j, sk).amin(dim=-1)                        # Sk when the row sees nothing
+    hi = torch.where(seen, j + 1, 0).amax(dim=-1)
+    in_range = (j >= lo[:, None]) & (j < hi[:, None])                 # [B', Sk]
+    lower = j[None, :] <= torch.arange(sq, device=dev)[:, None] + (sk - sq)   # [Sq, Sk]
+    want_c = lower[None] & in_range[:, None, :]
+    unmasked = keep.all(dim=-1, keepdim=True) & ~want_c.any(dim=-1, keepdim=True)
+    causal_ok = ((keep == want_c) | unmasked).all()
+    full_ok = (keep == in_range[:, None, :]).all()
+    flags = torch.stack([binary, causal_ok, full_ok]).to(torch.int64)
+    padded = ((lo != 0) | (hi != sk)).any().to(torch.int64)[None]
+    binary, causal_ok, full_ok, any_pad = (bool(v) for v in torch.cat([flags, padded]).tolist())
+    if not binary or not (causal_ok or full_ok):
+        return None
+    if not any_pad:
+        return causal_ok, None, None
+    lo = lo.to(torch.int32).expand(batch).contiguous()
+    hi = hi.to(torch.int32).expand(batch).contiguous()
+    return causal_ok, lo, hi
+
+
+def _is_plain_causal(mask: torch.Tensor, sq: int, sk: int) -> bool:
+    """True when a [B|1, 1, Sq, Sk] mask is the plain causal mask for every batch row."""
+    r = mask_key_ranges(mask, mask.shape[0] if mask.ndim == 4 else 1, sq, sk)
+    return r is not None and r[0] and r[1] is None
 
 
 def merge_max(running: torch.Tensor, new: torch.Tensor, valid: torch.Tensor | None) -> None:
@@ -246,8 +290,9 @@ def _probe_attention(module, query, key, value, attention_mask, scaling=None, dr
     (and its backward); while a QK-Clip capture is active, the library's max-logit kernel reads
     the same post-RoPE query and key states and records the per-head max of the pre-softmax
     logits. With MUZO_FUSED_ATTENTION=1, a capture call that qualifies (bf16/fp16, head dim 64 or
-    128, no gradient, no mask or the plain causal mask) runs one tensor-core kernel for the
-    output and the maxima instead (Q K^T formed once). Outside a capture it is SDPA alone."""
+    128, no gradient, no mask, the causal mask or a padding mask) runs one tensor-core kernel for
+    the output and the maxima instead (Q K^T formed once; a query row without a visible key gets
+    zeros, as SDPA returns for it). Outside a capture it is SDPA alone."""
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
 
     ctrl = _ACTIVE.get()
@@ -255,16 +300,20 @@ def _probe_attention(module, query, key, value, attention_mask, scaling=None, dr
         scaling = query.shape[-1] ** -0.5
     if ctrl is not None and os.environ.get("MUZO_FUSED_ATTENTION", "0") == "1":
         # one kernel for the attention and the capture when the call qualifies: no mask (the
-        # module's causality) or the plain causal mask. Off by default: on one Llama-3-70B layer
-        # it takes 0.52 ms against 0.37 ms for SDPA plus the separate max-logit kernel
+        # module's causality) or a causal / padding mask as key ranges. Off by default: on one Llama-3-70B layer
+        # it takes 0.43 ms against 0.37 ms for SDPA plus the separate max-logit kernel
         mask = attention_mask if attention_mask is not None and attention_mask.ndim == 4 else None
         sq = query.shape[2]
-        plain = mask is None or _is_plain_causal(mask, sq, key.shape[2])
+        ranges = None if mask is None else mask_key_ranges(mask, query.shape[0], sq, key.shape[2])
         name = ctrl.module_name(module)
-        if name is not None and plain and fused_attention_eligible(query, key, value, dropout):
-            causal = True if mask is not None else bool(getattr(module, "is_causal", True)) and sq > 1
+        if name is not None and (mask is None or ranges is not None) and \
+                fused_attention_eligible(query, key, value, dropout):
+            if ranges is None:
+                causal, lo, hi = bool(getattr(module, "is_causal", True)) and sq > 1, None, None
+            else:
+                causal, lo, hi = ranges
             with torch.no_grad():
-                out, smax, valid = attention_max(query, key, value, float(scaling), causal)
+                out, smax, valid = attention_max(query, key, value, float(scaling), causal, lo, hi)
             ctrl.record_max(name, smax, valid)
             return out, None
     if ctrl is not None:

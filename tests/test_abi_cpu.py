@@ -191,6 +191,9 @@ _P = 256
     (lambda L: L.muzo_qk_max(None, _P, 1, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 1),
     (lambda L: L.muzo_qk_max(_P, _P, 1, 1, 8, 3, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 1),  # GQA
     (lambda L: L.muzo_qk_max(_P, _P, 9, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, 1.0, _P, _P, None), 2),
+    (lambda L: L.muzo_qk_max_ranges(_P, _P, 1, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, _P, None, 1.0, _P, _P, None), 1),
+    (lambda L: L.muzo_qk_max_ranges(_P, _P, 1, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, None, _P, 1.0, _P, _P, None), 1),
+    (lambda L: L.muzo_qk_max_ranges(_P, _P, 9, 1, 8, 8, 16, 16, 128, 0, 0, 0, 0, 0, 0, 1, _P, _P, 1.0, _P, _P, None), 2),
     (lambda L: L.muzo_logits_head_max(_P, 1, 1, 70000, 4, 4, 0, 0, 0, 0, _P, _P, None), 1),
     (lambda L: L.muzo_logits_head_max(_P, 9, 1, 8, 4, 4, 0, 0, 0, 0, _P, _P, None), 2),
     (lambda L: L.muzo_max_merge(_P, _P, None, -1, None), 1),

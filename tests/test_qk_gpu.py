@@ -48,6 +48,54 @@ def test_qk_max_matches_eager_logits(device, qk_kernel, dtype, causal, b, hq, hk
     assert bool(((got - ref).abs() <= _ulp(ref, bits)).all()), (got, ref)
 
 
+def _padded_keep(lo, hi, sq, sk, causal, device):
+    j = torch.arange(sk, device=device)
+    rows = []
+    for a, b in zip(lo, hi):
+        r = ((j >= a) & (j < b))[None, :].expand(sq, sk)
+        if causal:
+            r = r & (j[None, :] <= torch.arange(sq, device=device)[:, None] + (sk - sq))
+        rows.append(r)
+    return torch.stack(rows)[:, None]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("form", ["bool", "additive"])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("b,hq,hkv,sq,sk,d,lo,hi", [
+    (3, 8, 2, 300, 300, 64, [0, 37, 0], [300, 300, 211]),         # none, left, right padding
+    (2, 4, 4, 1000, 1000, 128, [500, 0], [1000, 129]),             # long left / right padding
+    (2, 2, 1, 200, 460, 96, [259, 3], [460, 300]),                 # Sq < Sk, both sides
+    (2, 4, 1, 520, 520, 256, [0, 130], [520, 520]),                # head dim 256
+])
+def test_qk_max_with_padding_masks(device, qk_kernel, monkeypatch, dtype, form, causal, b, hq, hkv, sq, sk, d, lo,
+                                   hi):
+    """Padding masks (per batch row a range of visible keys, causal or not, in SDPA's boolean or
+    eager's additive form) run on the same kernels with per-batch key ranges: maxima equal the
+    eager capture's amax of logits + mask (qk_clip.py:186-196), without the S x S logits."""
+    from muzo_clip_b200 import _qk
+
+    g = torch.Generator(device="cpu").manual_seed(b * 7 + sq + d)
+    q = (torch.randn((b, sq, hq, d), generator=g) * 2).to(dtype).to(device).transpose(1, 2)
+    k = (torch.randn((b, sk, hkv, d), generator=g) * 2).to(dtype).to(device).transpose(1, 2)
+    scale = d ** -0.5
+    keep = _padded_keep(lo, hi, sq, sk, causal, device)
+    additive = torch.zeros(keep.shape, dtype=dtype, device=device).masked_fill(~keep, torch.finfo(dtype).min)
+    mask = keep if form == "bool" else additive
+
+    def no_logits(*a, **kw):
+        raise AssertionError("a padding mask must not materialise the logits")
+
+    monkeypatch.setattr(_qk, "logits_head_max", no_logits)
+    got, valid = _qk.qk_head_max(q, k, scale, True, mask)
+    torch.cuda.synchronize()
+    assert int(valid.item()) == 1
+    kr = k.repeat_interleave(hq // hkv, dim=1)
+    want = ((torch.matmul(q, kr.transpose(2, 3)) * scale) + additive).float().amax(dim=(0, 2, 3)).cpu()
+    bits = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 19}[dtype]
+    assert bool(((got.cpu() - want).abs() <= _ulp(want, bits)).all()), (got, want)
+
+
 @pytest.mark.parametrize("bad", [float("inf"), float("-inf"), float("nan")])
 def test_qk_max_flags_nonfinite(device, qk_kernel, bad):
     from muzo_clip_b200 import _qk

@@ -29,8 +29,8 @@ def test_plain_causal_test_is_cached_per_mask_and_version(monkeypatch):
     from muzo_clip_b200 import _qk
 
     calls = []
-    real = _qk._plain_causal_uncached
-    monkeypatch.setattr(_qk, "_plain_causal_uncached", lambda *a: calls.append(1) or real(*a))
+    real = _qk._key_ranges_uncached
+    monkeypatch.setattr(_qk, "_key_ranges_uncached", lambda *a: calls.append(1) or real(*a))
     i = torch.arange(5)[:, None]
     mask = torch.zeros(1, 1, 5, 5).masked_fill(torch.arange(5)[None, :] > i, torch.finfo(torch.float32).min)
     for _ in range(4):  # one mask, every layer of a forward
@@ -44,6 +44,77 @@ def test_plain_causal_test_is_cached_per_mask_and_version(monkeypatch):
     with torch.inference_mode():                                        # no version counter
         inf_mask = torch.zeros(1, 1, 2, 2)
     assert not _qk._is_plain_causal(inf_mask, 2, 2)
+
+
+def _padding_keep(lens_lo, lens_hi, sq, sk, causal):
+    """[B, 1, Sq, Sk] boolean mask: batch row b attends to keys [lo_b, hi_b) (and causally)."""
+    j = torch.arange(sk)
+    rows = []
+    for lo, hi in zip(lens_lo, lens_hi):
+        r = ((j >= lo) & (j < hi))[None, :].expand(sq, sk)
+        if causal:
+            r = r & _causal_keep(sq, sk)
+        rows.append(r)
+    return torch.stack(rows)[:, None]
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("form", ["bool", "additive_f32", "additive_bf16", "additive_f16"])
+def test_padding_masks_become_key_ranges(causal, form):
+    from muzo_clip_b200._qk import mask_key_ranges
+
+    sq = sk = 12
+    lo, hi = [0, 3, 0, 5], [12, 12, 9, 10]      # none, left, right, both
+    keep = _padding_keep(lo, hi, sq, sk, causal)
+    if form == "bool":
+        mask = keep
+    else:
+        dt = {"additive_f32": torch.float32, "additive_bf16": torch.bfloat16, "additive_f16": torch.float16}[
+            form]
+        mask = torch.zeros(keep.shape, dtype=dt).masked_fill(~keep, torch.finfo(dt).min)
+    r = mask_key_ranges(mask, 4, sq, sk)
+    assert r is not None
+    got_causal, got_lo, got_hi = r
+    assert got_causal == causal
+    assert got_lo.tolist() == lo and got_hi.tolist() == hi
+    assert got_lo.dtype == torch.int32 and got_lo.is_contiguous()
+
+
+def test_padding_mask_rows_without_keys_and_unmasked_rows():
+    """Left padding in a causal model: the padding queries see no key. transformers may let such
+    rows attend everywhere in SDPA's boolean form; both forms give the same ranges."""
+    from muzo_clip_b200._qk import mask_key_ranges
+
+    sq = sk = 8
+    keep = _padding_keep([0, 3], [8, 8], sq, sk, True)
+    unmasked = keep.clone()
+    unmasked[1, :, :3, :] = True
+    for m in (keep, unmasked):
+        causal, lo, hi = mask_key_ranges(m, 2, sq, sk)
+        assert causal and lo.tolist() == [0, 3] and hi.tolist() == [8, 8]
+
+
+def test_other_masks_are_not_key_ranges():
+    from muzo_clip_b200._qk import mask_key_ranges
+
+    sq = sk = 8
+    keep = _padding_keep([0, 0], [8, 8], sq, sk, True)
+    holes = keep.clone()
+    holes[0, :, :, 2] = False                    # a masked key inside the visible range
+    assert mask_key_ranges(holes, 2, sq, sk) is None
+    blocks = keep.clone()
+    blocks[:, :, 4:, :4] = False                 # block-diagonal (packed sequences)
+    assert mask_key_ranges(blocks, 2, sq, sk) is None
+    per_head = keep.expand(2, 3, sq, sk)         # a mask per head
+    assert mask_key_ranges(per_head, 2, sq, sk) is None
+    bias = torch.zeros(2, 1, sq, sk).masked_fill(~keep, -1e30)
+    bias[0, 0, 5, 1] = -0.5                      # a bias, not a mask
+    assert mask_key_ranges(bias, 2, sq, sk) is None
+    # one mask row for the whole batch expands to every batch row
+    causal, lo, hi = mask_key_ranges(_padding_keep([2], [7], sq, sk, False), 3, sq, sk)
+    assert not causal and lo.tolist() == [2, 2, 2] and hi.tolist() == [7, 7, 7]
+    # the plain causal mask: no ranges
+    assert mask_key_ranges(keep, 2, sq, sk) == (True, None, None)
 
 
 def test_boolean_mask_to_eager_form_remasks_unmasked_padding_rows():
