@@ -80,8 +80,12 @@ noalloc_prepare_kernel(NoallocScratch* s, int nsegs, int32_t* flags) {
     if (li >= numel) break;
     const int cnt = li + 8 <= numel ? 8 : static_cast<int>(numel - li);
     float v[8];
-    if (vec && cnt == 8) load8(in, li, DTYPE, v);
-    else for (int k = 0; k < 8; ++k) v[k] = k < cnt ? load_elem(in, li + k, DTYPE) : 0.0f;
+    if (vec && cnt == 8) {
+      load8(in, li, DTYPE, v);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = k < cnt ? load_elem(in, li + k, DTYPE) : 0.0f;
+    }
     float pm = 0.0f, px = 0.0f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -91,8 +95,13 @@ noalloc_prepare_kernel(NoallocScratch* s, int nsegs, int32_t* flags) {
       px = __fmaf_rn(xb, xb, px);
     }
     m2 += pm; x2 += px;
-    if (vec && cnt == 8) store8(out, li, MUZO_BF16, v);
-    else for (int k = 0; k < cnt; ++k) store_elem(out, li + k, MUZO_BF16, v[k]);
+    if (vec && cnt == 8) {
+      store8(out, li, MUZO_BF16, v);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < cnt) store_elem(out, li + k, MUZO_BF16, v[k]);
+    }
   }
   const double tm = cta_sum(m2);
   const double tx = cta_sum(x2);
@@ -134,25 +143,19 @@ noalloc_normalize_kernel(NoallocScratch* s, int nsegs, int32_t* flags) {
   }
 }
 
-// Device address of the scratch array, looked up once per device.
+// Device address of the scratch array in the current context, looked up on every call: a cached
+// address would dangle after the context is torn down and re-created (the module is reloaded
+// elsewhere), and the lookup costs little next to the three launches.
 NoallocScratch* scratch_for_current_device(int* status) {
-  static NoallocScratch* addr[64] = {nullptr};
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) { set_last_cuda_error(err); *status = MUZO_ERR_CUDA; return nullptr; }
-  if (dev < 0 || dev >= 64) { *status = MUZO_ERR_UNSUPPORTED; return nullptr; }
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (err != cudaSuccess || p == nullptr) {
-      set_last_cuda_error(err);
-      *status = MUZO_ERR_CUDA;
-      return nullptr;
-    }
-    addr[dev] = static_cast<NoallocScratch*>(p);
+  void* p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (err != cudaSuccess || p == nullptr) {
+    set_last_cuda_error(err);
+    *status = MUZO_ERR_CUDA;
+    return nullptr;
   }
   *status = MUZO_OK;
-  return addr[dev];
+  return static_cast<NoallocScratch*>(p);
 }
 
 }  // namespace
