@@ -15,10 +15,17 @@ to +-3, random 63-bit seeds. Synthetic data; 14 GB of weights, far larger than L
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 N > 1 runs under torchrun: every rank holds a replica, perturbs it locally, and rebuilds /
-orthogonalises / applies the matrices it owns (LPT partition by Newton-Schulz FLOPs); NCCL
-broadcasts the updated weights. ``--impl reference`` times the reference's op sequence on CPU
-tensors (one matrix per timed step, the four shape classes in turn) on the host cores,
-extrapolated to the full step.
+orthogonalises / applies the matrices it owns (LPT partition by Newton-Schulz FLOPs); the owners
+push the updated weights into the other ranks' replicas. ``--impl reference`` times the
+reference's op sequence on CPU tensors (one matrix per timed step, the four shape classes in
+turn) on the host cores, extrapolated to the full step.
+
+``--workload llama3-70b`` times the Llama-3-70B-shaped case instead (80 layers of q/o 8192x8192,
+k/v 1024x8192, gate/up 28672x8192, down 8192x28672: 68.4 G bf16 weights, 137 GB per replica, so
+no noise pool fits next to them): the same step with regenerated noise, then the QK-Clip probe
+over 80 layers (per-head max logit of synthetic Q [1, 64, 4096, 128] and K [1, 8, 4096, 128]
+activations per layer, causal, the maxima max-reduced over the ranks, the q/k rows scaled) through
+the optimizer's QK-Clip controller, without a model forward.
 """
 
 from __future__ import annotations
@@ -55,6 +62,16 @@ SHAPES = {
     "mlp.up_proj": (MLP, HIDDEN),
     "mlp.down_proj": (HIDDEN, MLP),
 }
+SHAPES_70B = {
+    "self_attn.q_proj": (8192, 8192),
+    "self_attn.k_proj": (1024, 8192),
+    "self_attn.v_proj": (1024, 8192),
+    "self_attn.o_proj": (8192, 8192),
+    "mlp.gate_proj": (28672, 8192),
+    "mlp.up_proj": (28672, 8192),
+    "mlp.down_proj": (8192, 28672),
+}
+LAYERS_70B = 80
 HORIZON = 8
 METRIC = "MuZO step() ms & perturb HBM GB/s, Llama-3-8B shapes, 1/2/4/8 B200"
 WORKLOAD = "llama3-8b-selected-matrices"
@@ -73,10 +90,13 @@ def ns_flops_total(layers: int = LAYERS, steps: int = 5) -> float:
 
 
 class Llama8BMatrices(torch.nn.Module):
-    """Selected-parameter skeleton of Llama-3-8B with HF names (no forward)."""
+    """Selected-parameter skeleton of a Llama model with HF names (no forward): Llama-3-8B
+    shapes unless ``shapes`` names others."""
 
-    def __init__(self, device, dtype=torch.bfloat16, layers: int = LAYERS, seed: int = 0):
+    def __init__(self, device, dtype=torch.bfloat16, layers: int = LAYERS, seed: int = 0,
+                 shapes: dict | None = None):
         super().__init__()
+        shapes = SHAPES if shapes is None else shapes
         g = torch.Generator(device=device).manual_seed(seed)
         self.model = torch.nn.Module()
         self.model.layers = torch.nn.ModuleList()
@@ -84,7 +104,7 @@ class Llama8BMatrices(torch.nn.Module):
             layer = torch.nn.Module()
             layer.self_attn = torch.nn.Module()
             layer.mlp = torch.nn.Module()
-            for name, (r, c) in SHAPES.items():
+            for name, (r, c) in shapes.items():
                 owner, leaf = name.split(".")
                 w = torch.empty((r, c), dtype=dtype, device=device)
                 w.normal_(0.0, 0.02, generator=g)
@@ -111,9 +131,20 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: wait (at most 3 s) for its first sample, so that a
+        # short timed region (a few steps of ~100 ms on 8 GPUs) is still sampled
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < 3.0 and self.proc.poll() is None:
+            try:
+                if self.path.stat().st_size > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
@@ -459,6 +490,92 @@ def run_gpu(args) -> int:
     return 0
 
 
+def run_70b(args) -> int:
+    """The Llama-3-70B-shaped step (regenerated noise) and the 80-layer QK-Clip probe."""
+    dist, rank, world, local = setup_dist()
+    device = torch.device("cuda", local)
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    layers = args.layers if args.layers is not None else LAYERS_70B
+    model = Llama8BMatrices(device, layers=layers, shapes=SHAPES_70B)
+    pg = dist.group.WORLD if dist is not None else None
+    opt = MuZOClipOptimizer(model, horizon=HORIZON, min_history=4, beta_momentum=0.9, lr=1e-5, seed=1234,
+                            process_group=pg, noise_cache=False, enable_qk_clip=True, qk_clip_tau=10.0)
+    run = _time_steps(opt, args, device, dist, local)
+    engine = opt._engine
+    phases, dev_ms = run["phases"], run["dev_ms"]
+    ns_ms = phases.get("ns", 0.0)
+    ns_tflops = engine.owned_ns_flops() / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+    ns_exec_tflops = engine.owned_ns_flops_executed() / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+
+    # QK-Clip probe: every rank captures its own batch's maxima (here synthetic activations),
+    # the controller max-reduces them over the group and scales the q/k rows
+    seq, hq, hkv, hd = 4096, 64, 8, 128
+    g = torch.Generator(device=device).manual_seed(100 + rank)
+    acts = []
+    for _ in range(layers):
+        q = (torch.randn((1, seq, hq, hd), generator=g, device=device, dtype=torch.bfloat16) * 1.5).transpose(1, 2)
+        k = (torch.randn((1, seq, hkv, hd), generator=g, device=device, dtype=torch.bfloat16) * 1.5).transpose(1, 2)
+        acts.append((q, k))
+    attn = [layer.self_attn for layer in model.model.layers]
+    ctrl = opt.qk_clip
+    stream = torch.cuda.current_stream(device)
+
+    def probe():
+        for module, (q, k) in zip(attn, acts):
+            ctrl.record_qk(module, q, k, hd ** -0.5, True, None)
+        return ctrl.apply()
+
+    for _ in range(2):
+        stats = probe()
+    reps = 3
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(reps):
+        stats = probe()
+    end.record(stream)
+    torch.cuda.synchronize()
+    probe_ms = start.elapsed_time(end) / reps
+    if dist is not None:
+        t = torch.tensor([probe_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        probe_ms = float(t.item())
+    probe_flops = 2.0 * hq * seq * (seq + 1) / 2.0 * hd * layers   # causal Q K^T
+
+    if rank == 0:
+        peaks = load_peaks()
+        line = {
+            "metric": "MuZO step() ms and QK-Clip probe ms, Llama-3-70B shapes",
+            "value": round(dev_ms, 3), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_ms, 3), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init bf16 weights of the named shapes, synthetic SPSA losses, synthetic Q/K)",
+            "config": {"workload": "llama3-70b-selected-matrices+qk-probe", "layers": layers,
+                       "matrices": len(engine.blocks), "elements": layers * sum(r * c for r, c in SHAPES_70B.values()),
+                       "horizon": HORIZON, "ns_steps": 5, "distribution": "normal", "noise_cache": False,
+                       "parallelism": f"replica perturb + NS partition x{world}",
+                       "probe": f"{layers} layers x B=1 S={seq} Hq={hq} Hkv={hkv} d={hd}, causal"},
+            "phase_ms": {k: round(v, 3) for k, v in phases.items()},
+            "other_ms": round(dev_ms - sum(phases.values()), 3),
+            "ns_tflops": round(ns_tflops, 1), "ns_executed_tflops": round(ns_exec_tflops, 1),
+            "ns_frac_of_sustained": round(ns_tflops / peaks["bf16_tflops_sustained"], 4),
+            "probe_ms": round(probe_ms, 3),
+            "probe_tflops": round(probe_flops / (probe_ms * 1e-3) / 1e12, 1),
+            "probe_clip_count": int(stats.qk_clip_count), "probe_smax_max": round(float(stats.qk_smax_max), 3),
+            "e2e": {"value": round(run["wall_ms"], 3), "unit": "ms/step"},
+            "gpu_launches": int(run["launches"]), "clocks": run["clocks"],
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_reference(args) -> int:
     """The reference's CPU implementation of the path on the host cores: every timed step is one
     matrix of one shape class (the classes in turn, so K steps cover all four when K >= 4), and the
@@ -729,7 +846,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="muzo", choices=["muzo", "reference"])
-    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--layers", type=int, default=None, help="layers (default 32, or 80 for llama3-70b)")
+    ap.add_argument("--workload", default="llama3-8b", choices=["llama3-8b", "llama3-70b"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--keep", action="store_true",
                     help="perturb case: a pass that reads kept noise (muzo_perturb_kept_noise); rebuild case: "
@@ -745,6 +863,10 @@ def main() -> int:
         return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "llama3-70b":
+        return run_70b(args)
+    if args.layers is None:
+        args.layers = LAYERS
     return run_gpu(args)
 
 

@@ -198,17 +198,34 @@ def pow_factors(gamma: np.ndarray, exponent: float, dtype: torch.dtype) -> np.nd
 
 def scale_rows(weight: torch.Tensor, groups: int, rows_per_group: int, factors: np.ndarray, mask: np.ndarray) -> None:
     """Rows of group g of ``weight`` *= factors[g] where mask[g] (qk_clip.py:289-308)."""
-    _check_cuda(weight)
-    if not weight.is_contiguous():
-        raise ValueError("QK-Clip scaling expects contiguous projection weights")
-    dev = weight.device
-    payload = np.concatenate([np.asarray(factors, np.float32).view(np.uint8),
-                              np.asarray(mask, np.int32).view(np.uint8)])
-    buf = torch.from_numpy(payload).to(dev)
-    fptr = buf.data_ptr()
-    mptr = fptr + 4 * int(groups)
-    _lib.launch("muzo_qk_scale_rows", weight.data_ptr(), _lib.dtype_code(weight.dtype), int(groups), int(rows_per_group),
-                                    int(weight.shape[1]), fptr, mptr, _lib.stream_ptr(dev))
+    scale_rows_many([(weight, groups, rows_per_group, factors, mask)])
+
+
+def scale_rows_many(jobs: list) -> None:
+    """Several row scalings ``(weight, groups, rows_per_group, factors, mask)``: the factors and
+    masks of all jobs on a device go up in one host-to-device copy, then one launch per weight
+    (a QK-Clip apply scales two matrices per attention layer: 160 for an 80-layer model)."""
+    by_device: dict = {}
+    for job in jobs:
+        weight = job[0]
+        _check_cuda(weight)
+        if not weight.is_contiguous():
+            raise ValueError("QK-Clip scaling expects contiguous projection weights")
+        by_device.setdefault(weight.device, []).append(job)
+    for dev, items in by_device.items():
+        parts, offsets, off = [], [], 0
+        for weight, groups, rows_per_group, factors, mask in items:
+            offsets.append(off)
+            parts.append(np.asarray(factors, np.float32).reshape(-1)[:groups].view(np.uint8))
+            parts.append(np.asarray(mask, np.int32).reshape(-1)[:groups].view(np.uint8))
+            off += 8 * int(groups)
+        buf = torch.from_numpy(np.concatenate(parts)).to(dev)
+        base = buf.data_ptr()
+        stream = _lib.stream_ptr(dev)
+        for (weight, groups, rows_per_group, _f, _m), o in zip(items, offsets):
+            fptr = base + o
+            _lib.launch("muzo_qk_scale_rows", weight.data_ptr(), _lib.dtype_code(weight.dtype), int(groups),
+                        int(rows_per_group), int(weight.shape[1]), fptr, fptr + 4 * int(groups), stream)
 
 
 # ---------------------------------------------------------------- fused attention

@@ -318,6 +318,7 @@ class QKClipController:
         fallback_used = False
         clip_count = 0
         smax_max = 0.0
+        jobs: list = []   # row scalings, launched together (their factors in one upload)
         for name, per_head in zip(names, host):
             module = self.modules.get(name)
             if module is None:
@@ -328,9 +329,11 @@ class QKClipController:
                 continue
             gamma = np.minimum(np.float32(self.tau) / np.maximum(per_head, np.float32(1e-12)),
                                np.float32(1.0)).astype(np.float32)
-            clipped, used_fallback = self._scale_qk(module.q_proj.weight, module.k_proj.weight, gamma, needs_clip)
+            clipped, used_fallback = self._scale_qk(module.q_proj.weight, module.k_proj.weight, gamma, needs_clip,
+                                                    jobs)
             clip_count += clipped
             fallback_used = fallback_used or used_fallback
+        _qk.scale_rows_many(jobs)
         self._captured_smax.clear()
         return QKClipApplyStats(True, True, fallback_used, None, smax_max, clip_count)
 
@@ -342,32 +345,33 @@ class QKClipController:
 
     @torch.no_grad()
     def _scale_qk(self, q_weight: torch.Tensor, k_weight: torch.Tensor, gamma: np.ndarray,
-                  needs_clip: np.ndarray) -> tuple[int, bool]:
+                  needs_clip: np.ndarray, jobs: list) -> tuple[int, bool]:
         """Per-head q rows * gamma^alpha, per kv-group k rows * (min gamma)^(1-alpha)
-        (qk_clip.py:262-310); whole-matrix fallback when the head layout does not divide."""
+        (qk_clip.py:262-310); whole-matrix fallback when the head layout does not divide. The
+        row scalings are appended to ``jobs``."""
         hq = int(gamma.size)
         if hq <= 0 or q_weight.ndim != 2 or k_weight.ndim != 2 or q_weight.shape[0] % hq != 0:
-            return self._scale_qk_fallback(q_weight, k_weight, gamma)
+            return self._scale_qk_fallback(q_weight, k_weight, gamma, jobs)
         hd = q_weight.shape[0] // hq
         if hd <= 0 or k_weight.shape[0] % hd != 0:
-            return self._scale_qk_fallback(q_weight, k_weight, gamma)
+            return self._scale_qk_fallback(q_weight, k_weight, gamma, jobs)
         hk = k_weight.shape[0] // hd
         if hk <= 0 or hq % hk != 0:
-            return self._scale_qk_fallback(q_weight, k_weight, gamma)
+            return self._scale_qk_fallback(q_weight, k_weight, gamma, jobs)
         q_factors = _qk.pow_factors(gamma, self.alpha, q_weight.dtype)
-        _qk.scale_rows(q_weight, hq, hd, q_factors, needs_clip)
+        jobs.append((q_weight, hq, hd, q_factors, needs_clip))
         group = hq // hk
         k_gamma = gamma.reshape(hk, group).min(axis=1)
         k_mask = needs_clip.reshape(hk, group).any(axis=1)
         k_factors = _qk.pow_factors(k_gamma, 1.0 - self.alpha, k_weight.dtype)
-        _qk.scale_rows(k_weight, hk, hd, k_factors, k_mask)
+        jobs.append((k_weight, hk, hd, k_factors, k_mask))
         return int(needs_clip.sum()) + int(k_mask.sum()), False
 
     @torch.no_grad()
     def _scale_qk_fallback(self, q_weight: torch.Tensor, k_weight: torch.Tensor,
-                           gamma: np.ndarray) -> tuple[int, bool]:
+                           gamma: np.ndarray, jobs: list) -> tuple[int, bool]:
         g = np.minimum(gamma.min(), np.float32(1.0)).astype(np.float32).reshape(1)
         one = np.ones(1, dtype=bool)
-        _qk.scale_rows(q_weight, 1, q_weight.shape[0], _qk.pow_factors(g, self.alpha, q_weight.dtype), one)
-        _qk.scale_rows(k_weight, 1, k_weight.shape[0], _qk.pow_factors(g, 1.0 - self.alpha, k_weight.dtype), one)
+        jobs.append((q_weight, 1, q_weight.shape[0], _qk.pow_factors(g, self.alpha, q_weight.dtype), one))
+        jobs.append((k_weight, 1, k_weight.shape[0], _qk.pow_factors(g, 1.0 - self.alpha, k_weight.dtype), one))
         return 2, True

@@ -185,7 +185,7 @@ def test_qk_scaling_host_logic_matches_reference(monkeypatch, dtype, hq, hkv, q_
     import muzo_clip_b200._qk as qk
     from muzo_clip_b200.qk_clip import QKClipController
 
-    monkeypatch.setattr(qk, "scale_rows", _cpu_scale_rows)
+    monkeypatch.setattr(qk, "scale_rows_many", lambda jobs: [_cpu_scale_rows(*job) for job in jobs])
     hd = 8
     mine_model = _attn_model(32, hq, hkv, hd, dtype)
     if q_rows is not None:  # a q projection whose rows do not split into the heads
