@@ -2,20 +2,23 @@
 // side output: QK-Clip's capture (qk_clip.py:173-196) computed by the attention that the forward
 // runs anyway, so Q K^T is formed once. Forward only (MuZO's forwards run without gradients).
 //
-// One CTA per (batch, query head, block of 128 queries), 11 warps:
-//   warp 0      TMA producer (one thread): the Q block once, then K tiles of 128 keys (K-major)
-//               into a 2-stage ring whose stage is free once S = Q K^T has read it;
-//   warp 10     TMA producer (one thread): V tiles of 128 keys (MN-major, the second operand of
-//               P V) into a 2-stage ring whose stage is free once P V has read it;
-//   warp 1      TMEM owner and MMA issuer (one thread): S_j = Q K_j^T (tcgen05.mma, fp32 in TMEM,
-//               two S buffers so S_{j+1} is computed while the softmax reads S_j), then
-//               O += P_j V_j into an fp32 accumulator that stays in TMEM;
-//   warps 2..9  softmax and epilogue, two warps per TMEM lane quarter (64 keys of a row each):
-//               the raw logits' running maximum (the side output, over visible logits only),
-//               the online softmax in base 2 with a lazy rescale (O and the row sum are rescaled
-//               only when the row maximum grows by more than 2^8), P in bf16/fp16 written to
-//               shared memory in the 128-byte swizzled K-major layout the MMA reads, and at the
-//               end O / l stored to [B, Sq, Hq, D].
+// One CTA per (batch, query head, block of 256 queries), 11 warps. The block is two query tiles
+// of 128 rows that share every K / V tile of 128 keys, so each K / V byte loaded serves 256 rows:
+//   warp 0      TMA producer (one thread): both query tiles once, then K tiles (K-major) into a
+//               1-stage ring, refilled once both tiles' S = Q K^T has read it (a stream's next S
+//               waits for its softmax anyway, so the load hides behind the softmax);
+//   warp 10     TMA producer (one thread): V tiles (MN-major, the second operand of P V) into a
+//               2-stage ring, refilled once both tiles' P V has read it;
+//   warp 1      TMEM owner and MMA issuer (one thread): per query tile s, S_s = Q_s K_j^T into
+//               its S buffer (fp32 in TMEM), then O_s += P_s V_j into its fp32 accumulator, which
+//               stays in TMEM;
+//   warps 2..9  two softmax streams of four warps, stream s for query tile s, one warp per TMEM
+//               lane quarter, one query row per thread, all 128 keys of each tile: the raw
+//               logits' maximum (the side output, over visible logits only), the online softmax
+//               in base 2 with a lazy rescale (O and the row sum are rescaled only when the row
+//               maximum grows by more than 2^8), P in bf16/fp16 written to shared memory in the
+//               128-byte swizzled K-major layout the MMA reads, and at the end O / l stored to
+//               [B, Sq, Hq, D]. The streams run side by side without waiting for each other.
 // Visibility: key j of batch b is visible to query i when key_lo[b] <= j < key_hi[b] (padding)
 // and, when causal, j <= i + Sk - Sq. Rows without a visible key are written as zeros.
 // Every wait is bounded; on timeout the kernel records a code in the status word, raises its
@@ -30,12 +33,13 @@ namespace {
 
 using namespace tc;
 
-constexpr int AM = 128;          // query rows per CTA (UMMA M)
+constexpr int AM = 128;          // query rows per query tile (UMMA M)
+constexpr int AMB = 2 * AM;      // query rows per CTA: two query tiles share each K / V tile
 constexpr int AN = 128;          // keys per tile: UMMA N of S, the K of P V
 constexpr int ABK = 64;          // 128-byte swizzle row of 16-bit elements
 constexpr int A_THREADS = 352;   // warp 0 TMA of Q and K, warp 1 MMA, warps 2..9 softmax (two streams
                                  // of four warps, one warp per TMEM lane quarter), warp 10 TMA of V
-constexpr int KV_STAGES = 2;     // one K and one V stage per softmax stream (tile j uses stage j % 2)
+constexpr int K_STAGES = 1;      // K ring depth (tile j uses K stage j % K_STAGES)
 constexpr int SUB_BYTES = 128 * ABK * 2;     // one swizzled block of 128 rows x 64 elements (16 KB)
 constexpr int BOX_BYTES = 64 * ABK * 2;      // one 64 x 64 box of the MN-major V operand (8 KB)
 constexpr uint32_t TMEM_COLS = 512;          // S of each stream at 0 and 128, O of each stream from 256
@@ -47,9 +51,11 @@ struct AttnLayout {
   static constexpr int K_BYTES = (D / ABK) * SUB_BYTES;
   static constexpr int V_BYTES = 2 * (D / ABK) * BOX_BYTES;
   static constexpr int P_BYTES = 2 * SUB_BYTES;   // one 128 x 128 P tile per stream
-  static constexpr int TILES_BYTES = Q_BYTES + KV_STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES;
+  // V ring depth: two stages next to two Q tiles, one K stage and two P tiles (224 KB for D = 128)
+  static constexpr int V_STAGES = 2;
+  static constexpr int TILES_BYTES = 2 * Q_BYTES + K_STAGES * K_BYTES + V_STAGES * V_BYTES + 2 * P_BYTES;
   static constexpr int BAR_BYTES = 256;           // barriers, TMEM address, flags
-  // tiles, barriers and 1 KB of alignment (224.25 KB for D = 128, within the 227 KB a CTA may
+  // tiles, barriers and 1 KB of alignment (225.25 KB for D = 128, within the 227 KB a CTA may
   // use); at least 116 KB so that one CTA holds an SM (every CTA allocates all 512 TMEM columns)
   static constexpr int NEED = TILES_BYTES + BAR_BYTES + 1024;
   static constexpr int SMEM_BYTES = NEED > 116 * 1024 ? NEED : 116 * 1024;
@@ -80,7 +86,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// Work item -> (batch, head, query block); the longest query blocks (last, when causal) first.
+// Work item -> (batch, head, block of 256 queries); the longest query blocks (last, when causal) first.
 __device__ __forceinline__ void attn_item(const AttnArgs& g, int64_t t, int& b, int& h, int& qb) {
   const int64_t bh_count = static_cast<int64_t>(g.batch) * g.hq;
   qb = g.nqb - 1 - static_cast<int>(t / bh_count);
@@ -89,25 +95,27 @@ __device__ __forceinline__ void attn_item(const AttnArgs& g, int64_t t, int& b, 
   h = static_cast<int>(bh % g.hq);
 }
 
-// First key tile and tile count of a work item.
+// First key tile of a work item and the tile counts of its two query tiles (zero for a tile with
+// no row inside the sequence or no visible key).
 __device__ __forceinline__ void attn_tiles(const AttnArgs& g, int b, int qb, int64_t& lo, int64_t& hi, int& t0,
-                                           int& ntiles) {
+                                           int& n0, int& n1) {
   lo = g.key_lo ? g.key_lo[b] : 0;
   hi = g.key_hi ? g.key_hi[b] : g.sk;
   if (lo < 0) lo = 0;
   if (hi > g.sk) hi = g.sk;
-  int64_t end = hi;
-  if (g.causal) {
-    const int64_t last = static_cast<int64_t>(qb) * AM + AM - 1 + g.shift + 1;  // keys the block's last row sees
-    if (last < end) end = last;
-  }
-  if (end <= lo) {
-    t0 = 0;
-    ntiles = 0;
-    return;
-  }
   t0 = static_cast<int>(lo / AN);
-  ntiles = static_cast<int>((end + AN - 1) / AN) - t0;
+  int n[2];
+  for (int t = 0; t < 2; ++t) {
+    const int64_t first = static_cast<int64_t>(qb) * AMB + t * AM;   // first row of query tile t
+    n[t] = 0;
+    if (first >= g.sq) continue;
+    const int64_t last_row = first + AM - 1 < g.sq - 1 ? first + AM - 1 : g.sq - 1;
+    int64_t end = hi;
+    if (g.causal && last_row + g.shift + 1 < end) end = last_row + g.shift + 1;  // keys the tile's last row sees
+    if (end > lo) n[t] = static_cast<int>((end + AN - 1) / AN) - t0;
+  }
+  n0 = n[0];
+  n1 = n[1];
 }
 
 // Three-input maximum (NaN-propagating) and minimum (sm_100).
@@ -128,22 +136,24 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
                     const __grid_constant__ CUtensorMap map_v, AttnArgs g) {
   using L = AttnLayout<D>;
   constexpr int NKB = D / ABK;   // 64-wide slices of the head dimension
+  constexpr int VS = L::V_STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  // K and V have rings of their own: a K stage is free once S_j = Q K_j^T is computed, long before
-  // P_j V_j frees the V stage. Tile j belongs to softmax stream j % 2 and uses K / V stage j % 2,
-  // the stream's S buffer, P buffer and O accumulator.
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + L::Q_BYTES;
-  uint8_t* sV = sK + KV_STAGES * L::K_BYTES;
-  uint8_t* sP = sV + KV_STAGES * L::V_BYTES;
+  // Two query tiles of 128 rows (streams 0 and 1) share every K / V tile of 128 keys: K through a
+  // 2-stage ring (a stage is free once both tiles' S has read it), V through a VS-stage ring (free
+  // once both tiles' P V has read it). Each stream owns an S buffer and an O accumulator in TMEM
+  // and a P tile in shared memory.
+  uint8_t* sQ = smem;                                   // [2][NKB][128 x 64]
+  uint8_t* sK = sQ + 2 * L::Q_BYTES;
+  uint8_t* sV = sK + K_STAGES * L::K_BYTES;
+  uint8_t* sP = sV + VS * L::V_BYTES;
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::TILES_BYTES);
   uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + KV_STAGES;
-  uint64_t* v_full = k_empty + KV_STAGES;
-  uint64_t* v_empty = v_full + KV_STAGES;
-  uint64_t* s_full = v_empty + KV_STAGES;   // [stream]: S of the stream's next tile computed
+  uint64_t* k_empty = k_full + K_STAGES;
+  uint64_t* v_full = k_empty + K_STAGES;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;          // [stream]: S of the stream's next tile computed
   uint64_t* p_full = s_full + 2;            // [stream]: P written (and S read) by the stream's 4 warps
   uint64_t* o_done = p_full + 2;            // [stream]: P V of the stream's last tile done
   uint64_t* drain = o_done + 2;
@@ -154,16 +164,15 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   int b, h, qb;
   attn_item(g, blockIdx.x, b, h, qb);
   int64_t lo, hi;
-  int t0, ntiles;
-  attn_tiles(g, b, qb, lo, hi, t0, ntiles);
+  int t0, n0, n1;
+  attn_tiles(g, b, qb, lo, hi, t0, n0, n1);
+  const int ntiles = n0 > n1 ? n0 : n1;   // K / V tiles loaded (stream 1's rows come later: n1 >= n0)
   const int kvh = h / g.group;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < KV_STAGES; ++s) {
-      mbar_init(k_full + s, 1); mbar_init(k_empty + s, 1);
-      mbar_init(v_full + s, 1); mbar_init(v_empty + s, 1);
-    }
+    for (int s = 0; s < K_STAGES; ++s) { mbar_init(k_full + s, 1); mbar_init(k_empty + s, 1); }
+    for (int s = 0; s < VS; ++s) { mbar_init(v_full + s, 1); mbar_init(v_empty + s, 1); }
     for (int s = 0; s < 2; ++s) { mbar_init(s_full + s, 1); mbar_init(p_full + s, 4); mbar_init(o_done + s, 1); }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -183,26 +192,29 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
 
   if (warp == 0 || warp == 10) {
     // ------------------------------------------------------------------ TMA producers
-    // warp 0: Q once, then K_j into K stage j % 2 once S_{j-2} has read it; warp 10: V_j into V
-    // stage j % 2 once P_{j-2} V_{j-2} has read it
+    // warp 0: both query tiles once, then K_j into K stage j % 2 once S_{j-2} of both streams has
+    // read it; warp 10: V_j into V stage j % VS once P_{j-VS} V_{j-VS} of both streams has read it
     if (lane == 0 && ntiles > 0) {
       const bool keys = warp == 0;
+      const int stages = keys ? K_STAGES : VS;
       uint64_t* full = keys ? k_full : v_full;
       uint64_t* empty = keys ? k_empty : v_empty;
       const uint32_t stage_bytes = keys ? L::K_BYTES : L::V_BYTES;
       if (keys) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
-        mbar_arrive_expect_tx(q_full, L::Q_BYTES);
-        for (int kb = 0; kb < NKB; ++kb) tma_load_4d(&map_q, q_full, sQ + kb * SUB_BYTES, kb * ABK, qb * AM, h, b);
+        mbar_arrive_expect_tx(q_full, 2 * L::Q_BYTES);
+        for (int t = 0; t < 2; ++t)
+          for (int kb = 0; kb < NKB; ++kb)
+            tma_load_4d(&map_q, q_full, sQ + t * L::Q_BYTES + kb * SUB_BYTES, kb * ABK, qb * AMB + t * AM, h, b);
       } else {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_v)) : "memory");
       }
       bool ok = true;
       uint32_t armed = 0, armed_parity = 0;
       for (int j = 0; j < ntiles; ++j) {
-        const int stage = j % KV_STAGES;
-        const uint32_t phase = static_cast<uint32_t>((j / KV_STAGES) & 1);
+        const int stage = j % stages;
+        const uint32_t phase = static_cast<uint32_t>((j / stages) & 1);
         if (!mbar_wait(empty + stage, phase ^ 1)) { ok = false; break; }
         if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(full + stage, stage_bytes);
@@ -226,24 +238,26 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       }
       // every load of this CTA must have landed before it may exit (bounded)
       if (keys) mbar_wait(q_full, 0);
-      for (int s2 = 0; s2 < KV_STAGES; ++s2)
+      for (int s2 = 0; s2 < stages; ++s2)
         if (armed & (1u << s2)) mbar_wait(full + s2, (armed_parity >> s2) & 1u);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    // S_0, S_1 first; then per tile j: once its stream's P_j is written, S_{j+2} (the stream's
-    // next logits, so its softmax can go on) and then O_s += P_j V_j.
+    // S_s(0) for both streams; then per tile j and stream s (in that order): once P_s(j) is
+    // written (S buffer s read), S_s(j + 1) and then O_s += P_s(j) V_j. A K stage is released after
+    // the last S that reads it, a V stage after the last P V.
     if (lane == 0 && ntiles > 0) {
       constexpr uint32_t idesc_s = make_idesc_fmt(AM, AN, false, false, FMT);
       constexpr uint32_t idesc_pv = make_idesc_fmt(AM, D, false, true, FMT);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(k_full + s, static_cast<uint32_t>((j >> 1) & 1))) return false;
+      const int nt[2] = {n0, n1};
+      auto issue_s = [&](int s, int j) -> bool {
+        const int stage = j % K_STAGES;
+        if (!mbar_wait(k_full + stage, static_cast<uint32_t>((j / K_STAGES) & 1))) return false;
         if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
         tc_fence_after();
-        const uint32_t sq_ = smem_u32(sQ);
-        const uint32_t sk_ = smem_u32(sK + s * L::K_BYTES);
+        const uint32_t sq_ = smem_u32(sQ + s * L::Q_BYTES);
+        const uint32_t sk_ = smem_u32(sK + stage * L::K_BYTES);
 #pragma unroll
         for (int kb = 0; kb < NKB; ++kb)
 #pragma unroll
@@ -251,16 +265,16 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
             umma_f16(tmem_base + s * AN, make_sdesc(sq_ + kb * SUB_BYTES + k * 32, 16, 1024),
                      make_sdesc(sk_ + kb * SUB_BYTES + k * 32, 16, 1024), idesc_s, (kb > 0 || k > 0) ? 1u : 0u);
         umma_commit(s_full + s);
-        umma_commit(k_empty + s);   // K_j read
+        // the last stream that reads K_j (stream 1 whenever it has tile j) releases the stage
+        if (s == 1 || j >= nt[1]) umma_commit(k_empty + stage);
         return true;
       };
-      auto issue_pv = [&](int j) -> bool {
-        const int s = j & 1;
-        const uint32_t use = static_cast<uint32_t>(j >> 1);
-        if (!mbar_wait(v_full + s, use & 1u)) return false;
+      auto issue_pv = [&](int s, int j) -> bool {
+        const int stage = j % VS;
+        if (!mbar_wait(v_full + stage, static_cast<uint32_t>((j / VS) & 1))) return false;
         if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
         tc_fence_after();
-        const uint32_t sv = smem_u32(sV + s * L::V_BYTES);
+        const uint32_t sv = smem_u32(sV + stage * L::V_BYTES);
         const uint32_t sp = smem_u32(sP + s * L::P_BYTES);
 #pragma unroll
         for (int kc = 0; kc < 2; ++kc)
@@ -268,19 +282,22 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
           for (int k = 0; k < ABK / 16; ++k)
             umma_f16(tmem_o + s * D, make_sdesc(sp + kc * SUB_BYTES + k * 32, 16, 1024),
                      make_sdesc(sv + kc * NKB * BOX_BYTES + k * (16 * 128), BOX_BYTES, 1024), idesc_pv,
-                     (use > 0 || kc > 0 || k > 0) ? 1u : 0u);
-        umma_commit(v_empty + s);   // V_j read
-        umma_commit(o_done + s);    // P buffer of the stream free, O_s holds its tiles up to j
+                     (j > 0 || kc > 0 || k > 0) ? 1u : 0u);
+        if (s == 1 || j >= nt[1]) umma_commit(v_empty + stage);   // V_j read by both streams
+        umma_commit(o_done + s);        // P buffer of the stream free, O_s holds its tiles up to j
         return true;
       };
       bool ok = mbar_wait(q_full, 0);
-      if (ok) ok = issue_s(0);
-      if (ok && ntiles > 1) ok = issue_s(1);
+      for (int s = 0; s < 2 && ok; ++s)
+        if (nt[s] > 0) ok = issue_s(s, 0);
       for (int j = 0; j < ntiles && ok; ++j) {
-        if (!mbar_wait(p_full + (j & 1), static_cast<uint32_t>((j >> 1) & 1))) { ok = false; break; }
-        tc_fence_after();
-        if (j + 2 < ntiles && !issue_s(j + 2)) { ok = false; break; }
-        if (!issue_pv(j)) { ok = false; break; }
+        for (int s = 0; s < 2 && ok; ++s) {
+          if (j >= nt[s]) continue;
+          if (!mbar_wait(p_full + s, static_cast<uint32_t>(j & 1))) { ok = false; break; }
+          tc_fence_after();
+          if (j + 1 < nt[s] && !issue_s(s, j + 1)) { ok = false; break; }
+          if (!issue_pv(s, j)) { ok = false; break; }
+        }
       }
       if (!ok) {
         atomicCAS(g.status, kErrNone, kErrTimeoutMma);
@@ -291,36 +308,33 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax streams and epilogue
-    // Stream s (warps 2..5: s = 0, warps 6..9: s = 1) takes tiles j = s, s + 2, ...: one warp per
-    // TMEM lane quarter, one query row per thread, all 128 keys of the tile. Each stream keeps its
-    // own running maximum, row sum and O accumulator; they are combined once at the end. The two
-    // streams do not wait for each other, so one computes exponentials while the other is in its
-    // maximum pass, and each stream's next S is computed while it works on the current one.
+    // Stream s (warps 2..5: s = 0, warps 6..9: s = 1) owns query tile s of the block: one warp per
+    // TMEM lane quarter, one query row per thread, all 128 keys of each tile. The two streams run
+    // side by side on the same K / V tiles without waiting for each other.
     const int quarter = warp & 3;
     const int stream = (warp - 2) >> 2;
-    const int r = 32 * quarter + lane;                 // row of the block == TMEM lane
-    const int64_t row = static_cast<int64_t>(qb) * AM + r;
+    const int r = 32 * quarter + lane;                 // row of the tile == TMEM lane
+    const int64_t row = static_cast<int64_t>(qb) * AMB + stream * AM + r;
     const bool row_in = row < g.sq;
     const int64_t jmax = g.causal ? row + g.shift : g.sk - 1;  // last key visible by causality
     const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
     const uint32_t s_cols = tmem_base + lane_addr + stream * AN;
     const uint32_t o_cols = tmem_o + lane_addr + stream * D;
     uint8_t* my_p = sP + stream * L::P_BYTES;
-    const int n_mine = (ntiles - stream + 1) / 2;      // tiles of this stream
+    const int n_mine = stream == 0 ? n0 : n1;
     float m_run = -INFINITY;    // running maximum of the scaled logits (log2 units) used by P
-    float l_run = 0.0f;         // running sum of P over this stream's tiles
+    float l_run = 0.0f;         // running sum of P
     float raw_max = -INFINITY;  // side output: maximum of the visible raw logits q . k (NaN-propagating)
     float raw_min = INFINITY;   // a visible -inf logit shows here
     bool ok = true;
     for (int u = 0; u < n_mine; ++u) {
-      const int j = 2 * u + stream;
       bool ready = true;
       if (lane == 0) ready = mbar_wait(s_full + stream, static_cast<uint32_t>(u & 1));
       ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
       if (!ready || *reinterpret_cast<volatile int*>(abort_flag)) { ok = false; break; }
       tc_fence_after();
       // visible key columns [c_lo, c_hi) of this tile for this row
-      const int64_t key0 = static_cast<int64_t>(t0 + j) * AN;
+      const int64_t key0 = static_cast<int64_t>(t0 + u) * AN;
       const int64_t end = hi < jmax + 1 ? hi : jmax + 1;
       int c_lo = 0, c_hi = 0;
       if (row_in) {
@@ -437,7 +451,7 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full + stream);
     }
-    // this stream's last P V must be done before O_s is read and its P buffer is reused
+    // this stream's last P V must be done before O_s is read
     if (ok && n_mine > 0) {
       bool done = true;
       if (lane == 0) done = mbar_wait(o_done + stream, static_cast<uint32_t>((n_mine - 1) & 1));
@@ -445,47 +459,28 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       if (!done) ok = false;
       tc_fence_after();
     }
-    // combine the two streams of each row: the warps of a TMEM lane quarter (one per stream)
-    // exchange (m, l, ok) through their P buffers and each writes half of the row's columns of
-    // O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m))
-    float* xch = reinterpret_cast<float*>(my_p);
-    xch[r] = m_run;
-    xch[AM + r] = l_run;
-    reinterpret_cast<int*>(xch)[2 * AM + r] = ok ? 1 : 0;
-    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
-    const float* other = reinterpret_cast<const float*>(sP + (stream ^ 1) * L::P_BYTES);
-    const float m_o = other[r], l_o = other[AM + r];
-    ok = ok && reinterpret_cast<const int*>(other)[2 * AM + r] != 0;
-    const int n_other = (ntiles - (stream ^ 1) + 1) / 2;
-    if (__all_sync(0xffffffffu, ok)) {
-      const float m_all = fmaxf(m_run, m_o);
-      const float a_me = m_run == -INFINITY ? 0.0f : fast_exp2(m_run - m_all);
-      const float a_ot = m_o == -INFINITY ? 0.0f : fast_exp2(m_o - m_all);
-      const float l_total = l_run * a_me + l_o * a_ot;
-      const float inv = l_total > 0.0f ? 1.0f / l_total : 0.0f;
-      const float w0 = (stream == 0 ? a_me : a_ot) * inv;   // weight of O_0
-      const float w1 = (stream == 0 ? a_ot : a_me) * inv;   // weight of O_1
-      const bool have0 = (stream == 0 ? n_mine : n_other) > 0;
-      const bool have1 = (stream == 0 ? n_other : n_mine) > 0;
-      constexpr int HD = D / 2;   // output columns per warp
+    if (ok) {
+      // O / l of this row (zeros for a row without a visible key or a tile without one)
+      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
       uint16_t* orow = reinterpret_cast<uint16_t*>(g.out) + static_cast<int64_t>(b) * g.o_sb +
-                       static_cast<int64_t>(h) * g.o_sh + row * g.o_ss + stream * HD;
+                       static_cast<int64_t>(h) * g.o_sh + row * g.o_ss;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t v0[32], v1[32];
-        const uint32_t col = lane_addr + stream * HD + c * 32;
-        if (have0) tmem_ld32(tmem_o + col, v0);
-        if (have1) tmem_ld32(tmem_o + D + col, v1);
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        if (n_mine > 0) {
+          tmem_ld32(o_cols + c * 32, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = 0u;
+        }
         if (row_in) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const int i0 = 8 * q + 2 * e;
-              float o0 = 0.0f, o1 = 0.0f;
-              if (have0) { o0 = __uint_as_float(v0[i0]) * w0; o1 = __uint_as_float(v0[i0 + 1]) * w0; }
-              if (have1) { o0 = fmaf(__uint_as_float(v1[i0]), w1, o0); o1 = fmaf(__uint_as_float(v1[i0 + 1]), w1, o1); }
+              const float o0 = __uint_as_float(v[8 * q + 2 * e]) * inv;
+              const float o1 = __uint_as_float(v[8 * q + 2 * e + 1]) * inv;
               w[e] = FMT == 1 ? pack_bf16(o0, o1) : pack_half(o0, o1);
             }
             *reinterpret_cast<uint4*>(orow + c * 32 + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -609,7 +604,7 @@ int muzo_attention_max(const void* q, const void* k, const void* v, void* out, i
   int* enc = reinterpret_cast<int*>(smax);
   if (enc != nullptr)
     init_attn_max_kernel<<<static_cast<unsigned>((hq + 255) / 256), 256, 0, s>>>(enc, static_cast<int>(hq), d_valid);
-  const int64_t nqb = (seq_q + AM - 1) / AM;
+  const int64_t nqb = (seq_q + AMB - 1) / AMB;
   const int64_t items = batch * hq * nqb;
   if (items > 0) {
     if (items > 0x7fffffffLL) return MUZO_ERR_UNSUPPORTED;

@@ -318,7 +318,7 @@ def _probe_attention(module, query, key, value, attention_mask, scaling=None, dr
     if ctrl is not None and os.environ.get("MUZO_FUSED_ATTENTION", "0") == "1":
         # one kernel for the attention and the capture when the call qualifies: no mask (the
         # module's causality) or a causal / padding mask as key ranges. Off by default: on one Llama-3-70B layer
-        # it takes 0.43 ms against 0.37 ms for SDPA plus the separate max-logit kernel
+        # it takes 0.378 ms, level with SDPA plus the separate max-logit kernel (0.377 ms)
         mask = attention_mask if attention_mask is not None and attention_mask.ndim == 4 else None
         sq = query.shape[2]
         ranges = None if mask is None else mask_key_ranges(mask, query.shape[0], sq, key.shape[2])
