@@ -157,7 +157,8 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   uint64_t* p_full = s_full + 2;            // [stream]: P written (and S read) by the stream's 4 warps
   uint64_t* o_done = p_full + 2;            // [stream]: P V of the stream's last tile done
   uint64_t* drain = o_done + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* stall_bar = drain + 1;          // nothing arrives here: a stall request waits on it
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(stall_bar + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -168,6 +169,8 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
   attn_tiles(g, b, qb, lo, hi, t0, n0, n1);
   const int ntiles = n0 > n1 ? n0 : n1;   // K / V tiles loaded (stream 1's rows come later: n1 >= n0)
   const int kvh = h / g.group;
+  // status word 1: a role (1 producer, 2 MMA, 3 softmax) whose first wait is made to expire
+  const int stall = *reinterpret_cast<volatile int*>(g.status + 1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -175,6 +178,7 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     for (int s = 0; s < VS; ++s) { mbar_init(v_full + s, 1); mbar_init(v_empty + s, 1); }
     for (int s = 0; s < 2; ++s) { mbar_init(s_full + s, 1); mbar_init(p_full + s, 4); mbar_init(o_done + s, 1); }
     mbar_init(drain, 1);
+    mbar_init(stall_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -200,19 +204,20 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
       uint64_t* full = keys ? k_full : v_full;
       uint64_t* empty = keys ? k_empty : v_empty;
       const uint32_t stage_bytes = keys ? L::K_BYTES : L::V_BYTES;
-      if (keys) {
+      bool ok = !(keys && stall == kErrTimeoutProducer && !mbar_wait(stall_bar, 0, kStallLimitCycles));
+      if (keys && ok) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_q)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
         mbar_arrive_expect_tx(q_full, 2 * L::Q_BYTES);
         for (int t = 0; t < 2; ++t)
           for (int kb = 0; kb < NKB; ++kb)
             tma_load_4d(&map_q, q_full, sQ + t * L::Q_BYTES + kb * SUB_BYTES, kb * ABK, qb * AMB + t * AM, h, b);
-      } else {
+      } else if (!keys) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_v)) : "memory");
       }
-      bool ok = true;
+      const bool q_armed = keys && ok;
       uint32_t armed = 0, armed_parity = 0;
-      for (int j = 0; j < ntiles; ++j) {
+      for (int j = 0; j < ntiles && ok; ++j) {
         const int stage = j % stages;
         const uint32_t phase = static_cast<uint32_t>((j / stages) & 1);
         if (!mbar_wait(empty + stage, phase ^ 1)) { ok = false; break; }
@@ -237,7 +242,7 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         if (g.valid) atomicExch(g.valid, 0);
       }
       // every load of this CTA must have landed before it may exit (bounded)
-      if (keys) mbar_wait(q_full, 0);
+      if (q_armed) mbar_wait(q_full, 0);
       for (int s2 = 0; s2 < stages; ++s2)
         if (armed & (1u << s2)) mbar_wait(full + s2, (armed_parity >> s2) & 1u);
     }
@@ -287,7 +292,8 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
         umma_commit(o_done + s);        // P buffer of the stream free, O_s holds its tiles up to j
         return true;
       };
-      bool ok = mbar_wait(q_full, 0);
+      bool ok = stall != kErrTimeoutMma || mbar_wait(stall_bar, 0, kStallLimitCycles);
+      ok = ok && mbar_wait(q_full, 0);
       for (int s = 0; s < 2 && ok; ++s)
         if (nt[s] > 0) ok = issue_s(s, 0);
       for (int j = 0; j < ntiles && ok; ++j) {
@@ -327,7 +333,12 @@ attn_fwd_max_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_cons
     float raw_max = -INFINITY;  // side output: maximum of the visible raw logits q . k (NaN-propagating)
     float raw_min = INFINITY;   // a visible -inf logit shows here
     bool ok = true;
-    for (int u = 0; u < n_mine; ++u) {
+    if (stall == kErrTimeoutEpilogue) {
+      bool waited = true;
+      if (lane == 0) waited = mbar_wait(stall_bar, 0, kStallLimitCycles);
+      ok = __shfl_sync(0xffffffffu, waited ? 1 : 0, 0) != 0;
+    }
+    for (int u = 0; u < n_mine && ok; ++u) {
       bool ready = true;
       if (lane == 0) ready = mbar_wait(s_full + stream, static_cast<uint32_t>(u & 1));
       ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;

@@ -79,9 +79,7 @@ struct GemmArgs {
   int32_t* flags;
 };
 
-// Stall request read from status word 3 at kernel start (test use): the named role waits on a
-// barrier nothing arrives at, for kStallLimitCycles, and then takes the timeout path.
-constexpr unsigned long long kStallLimitCycles = kWaitLimitCycles / 8;
+// Stall request read from status word 3 at kernel start (test use), see kStallLimitCycles.
 
 // Sum of squares of the stored (bf16-rounded) values times `scale`, in the order of the separate
 // update_sumsq pass: an fp32 chain over each 8 values, added in fp64.

@@ -12,6 +12,9 @@ namespace muzo {
 namespace tc {
 
 constexpr unsigned long long kWaitLimitCycles = 4ull * 1000 * 1000 * 1000;  // ~2 s at 2 GHz
+// A stall request (test use: a status word a kernel reads at start) makes the named role wait on
+// a barrier nothing arrives at, for kStallLimitCycles, and then take the timeout path.
+constexpr unsigned long long kStallLimitCycles = kWaitLimitCycles / 8;
 
 enum : int { kErrNone = 0, kErrTimeoutProducer = 1, kErrTimeoutMma = 2, kErrTimeoutEpilogue = 3 };
 

@@ -234,11 +234,12 @@ _ATTN_STATUS: dict[int, torch.Tensor] = {}
 
 
 def attention_status(device: torch.device) -> torch.Tensor:
-    """One device int32 per GPU: the first nonzero timeout code of a fused attention launch."""
+    """Two device int32 words per GPU: [0] the first nonzero timeout code of a fused attention
+    launch, [1] the stall request (0; tests set a role's code to make its first wait expire)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _ATTN_STATUS.get(idx)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=device)
+        t = torch.zeros(2, dtype=torch.int32, device=device)
         _ATTN_STATUS[idx] = t
     return t
 
@@ -249,9 +250,9 @@ def check_attention_status(device: torch.device) -> None:
         return
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _ATTN_STATUS.get(idx)
-    if t is not None and int(t.item()) != 0:
-        code = int(t.item())
-        t.zero_()
+    if t is not None and int(t[0].item()) != 0:
+        code = int(t[0].item())
+        t[0].zero_()
         raise _lib.MuzoError(f"fused attention reported status {code} (a bounded wait expired); the outputs of "
                              "the forward that ran it are unspecified")
 

@@ -156,3 +156,35 @@ def test_fused_attention_flags_nonfinite_logits(device):
     q[0, 1, 3, 5] = float("inf")
     _, _, valid = _qk.attention_max(q, k, v, 0.125, True)
     assert int(valid.item()) == 0
+
+
+@pytest.mark.parametrize("role", [1, 2, 3])
+def test_fused_attention_bounded_waits_expire(device, role):
+    """A stall request (status word 1) makes one role's first wait expire: the producer (1), the
+    MMA issuer (2) or the softmax warps (3). The kernel records that role's code, drains its loads
+    and MMAs, frees TMEM and returns; the Python check raises; the next launch on the same context
+    computes the right result."""
+    from muzo_clip_b200 import _lib, _qk
+
+    g = torch.Generator(device="cpu").manual_seed(5)
+    q = torch.randn((1, 300, 2, 64), generator=g).to(torch.bfloat16).to(device).transpose(1, 2)
+    k = torch.randn((1, 300, 2, 64), generator=g).to(torch.bfloat16).to(device).transpose(1, 2)
+    v = torch.randn((1, 300, 2, 64), generator=g).to(torch.bfloat16).to(device).transpose(1, 2)
+    status = _qk.attention_status(device)
+    status.zero_()
+    status[1] = role
+    try:
+        _qk.attention_max(q, k, v, 0.125, True)
+        torch.cuda.synchronize()
+        assert int(status[0].item()) == role
+        with pytest.raises(_lib.MuzoError):
+            _qk.check_attention_status(device)
+        assert int(status[0].item()) == 0
+    finally:
+        status[1] = 0
+    out, smax, valid = _qk.attention_max(q, k, v, 0.125, True)
+    torch.cuda.synchronize()
+    _qk.check_attention_status(device)
+    ref, vis = _reference(q, k, v, 0.125, True)
+    assert float((out.float() - ref).abs().max()) <= 3e-2
+    assert int(valid.item()) == 1
