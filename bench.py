@@ -649,6 +649,27 @@ SWEEPS = {
 }
 
 
+def _cpu_ns_baseline(rows: int, cols: int, batch: int) -> dict:
+    """The reference's CPU Newton-Schulz (fp32) for one matrix of the shape, scaled to the batch;
+    the 8192 x 28672 shape (about 3 minutes per matrix on 16 cores) is extrapolated by FLOPs from
+    4096 x 14336, the same aspect ratio."""
+    from muzo_clip_b200._engine import ns_flops
+
+    cb = _cpu_baseline_module()
+    threads = cb.use_all_threads()
+    cb.ns_seconds(256, 256)                                                    # warm-up
+    if rows * cols > 4096 * 14336:
+        r0, c0 = (4096, 14336) if cols >= rows else (14336, 4096)
+        sec = cb.ns_seconds(r0, c0) * ns_flops(rows, cols, 5) / ns_flops(r0, c0, 5)
+        sample = f"one {r0}x{c0} matrix timed, extrapolated by FLOPs to {rows}x{cols}, x{batch}"
+    else:
+        sec = cb.ns_seconds(rows, cols)
+        sample = f"one {rows}x{cols} matrix timed, x{batch}"
+    return {"value": round(sec * batch * 1e3, 1), "unit": "ms per batch", "cores": threads, "kind": "port",
+            "dense_tflops": round(batch * ns_flops(rows, cols, 5) / (sec * batch) / 1e12, 3),
+            "sample": f"the reference's Newton-Schulz (CPU branch, fp32) on CPU tensors: {sample}"}
+
+
 def run_case(args) -> int:
     if not args.sweep:
         return _run_one_case(args)
@@ -687,6 +708,8 @@ def _run_one_case(args) -> int:
         fl = args.batch * ns_flops(args.rows, args.cols, 5)
         out.update(rows=args.rows, cols=args.cols, batch=args.batch, symmetric=not args.dense, ms=round(ms, 3),
                    dense_tflops=round(fl / ms / 1e9, 1), status=int(status[0]))
+        if args.sweep and not args.no_cpu_baseline:
+            out["cpu_baseline"] = _cpu_ns_baseline(args.rows, args.cols, args.batch)
     elif args.case in ("perturb", "rebuild", "apply", "normalize"):
         numel = args.numel
         cols = 4096 if numel % 4096 == 0 else 1
@@ -778,6 +801,16 @@ def _run_one_case(args) -> int:
                    horizon=args.horizon if args.case == "rebuild" else None,
                    ms=round(ms, 4), gbs=round(gbs, 1), hbm_frac=round(gbs / peaks["hbm_gbs"], 4),
                    l2="flushed between passes" if flush is not None else "working set larger than L2")
+        if args.case == "perturb" and args.sweep and not args.keep and not args.no_cpu_baseline \
+                and numel <= (256 << 20):
+            cb = _cpu_baseline_module()
+            threads = cb.use_all_threads()
+            cb.perturb_pass_seconds(min(numel, 1 << 20), args.dist)          # warm-up
+            cpu_s = statistics.median(cb.perturb_pass_seconds(numel, args.dist, i) for i in range(3))
+            out["cpu_baseline"] = {"value": round(cpu_s * 1e3, 3), "unit": "ms per pass", "cores": threads,
+                                   "kind": "port", "gbs": round(4.0 * numel / cpu_s / 1e9, 2),
+                                   "sample": f"the reference's perturbation op sequence on CPU tensors ({args.dist} "
+                                             f"noise from the CPU generator), median of 3 passes"}
     elif args.case == "attn":
         # one attention layer with the per-head max-logit side output (the fused capture path)
         # against SDPA plus the separate max-logit kernel on the same states

@@ -88,3 +88,26 @@ def describe(samples: dict[int, list[float]], threads: int) -> str:
             f"{os.cpu_count()}): one bf16 matrix per sample through 3 perturbation passes, the H=8 "
             f"normal-noise rebuild, fp32 Newton-Schulz (the reference's CPU branch) and the update; "
             f"{'; '.join(parts)}; the 224-matrix step extrapolated by count from each class's median")
+
+
+@torch.no_grad()
+def ns_seconds(rows: int, cols: int, seed: int = 0) -> float:
+    """Seconds of the reference's Newton-Schulz (five iterations, its CPU branch: fp32) on one
+    fp32 N(0, 1) matrix of rows x cols (the sweep of configuration 3 times one matrix per shape)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((rows, cols), generator=g)
+    t0 = time.perf_counter()
+    tr.newton_schulz(x, 5)
+    return time.perf_counter() - t0
+
+
+@torch.no_grad()
+def perturb_pass_seconds(numel: int, dist: str = "rademacher", seed: int = 0) -> float:
+    """Seconds of one perturbation pass of the reference's op sequence (noise generated on the
+    CPU, W <- bf16(W + eps * Z)) over a flat bf16 tensor [numel / 4096, 4096]."""
+    g = torch.Generator().manual_seed(seed)
+    w = (torch.randn((numel // 4096, 4096), generator=g) * 0.02).to(torch.bfloat16)
+    named = [("model.layers.0.mlp.up_proj.weight", w)]
+    t0 = time.perf_counter()
+    tr.perturb(named, 12345 + seed, 1.0, 1e-3, dist)
+    return time.perf_counter() - t0
