@@ -670,6 +670,73 @@ def _cpu_ns_baseline(rows: int, cols: int, batch: int) -> dict:
             "sample": f"the reference's Newton-Schulz (CPU branch, fp32) on CPU tensors: {sample}"}
 
 
+def _config1_model(device):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(1234)
+    cfg = LlamaConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=4,
+                      intermediate_size=688, vocab_size=1024, attn_implementation="eager", initializer_range=0.02)
+    return LlamaForCausalLM(cfg).float().to(device)
+
+
+def _config1_run(opt_cls, device, sync) -> tuple[float, float, int]:
+    """Configuration 1 through the public API: the tiny Llama (2 layers, hidden 256, 4 heads, MLP
+    688, vocab 1024, fp32), batch 4 x 64 token ids, default hyperparameters, normal noise, 20 SPSA
+    steps and one QK-Clip probe. Returns (seconds for the 20 steps, seconds for the probe, steps
+    not skipped)."""
+    model = _config1_model(device)
+    ids = torch.randint(0, 1024, (4, 64), generator=torch.Generator().manual_seed(0)).to(device)
+    opt = opt_cls(model, enable_qk_clip=True, seed=1234)
+
+    def closure():
+        with torch.no_grad():
+            return model(input_ids=ids, labels=ids).loss
+
+    sync()
+    t0 = time.perf_counter()
+    done = 0
+    for _ in range(20):
+        opt.estimate_projection(closure)
+        done += 0 if opt.step()["skipped"] else 1
+    sync()
+    t1 = time.perf_counter()
+    opt.probe_and_apply_qk_clip(closure, force_eager=True)
+    sync()
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1, done
+
+
+def _run_config1(device) -> dict:
+    """This build on the GPU and the reference package itself (``baseline/_ref``, or
+    MUZO_REFERENCE_PATH) on the host cores, both through the reference's public API."""
+    from muzo_clip_b200 import MuZOClipOptimizer
+
+    sync = torch.cuda.synchronize
+    _config1_run(MuZOClipOptimizer, device, sync)                    # warm-up (kernels, transformers)
+    gpu_s, gpu_probe_s, gpu_done = _config1_run(MuZOClipOptimizer, device, sync)
+    res = {"workload": "tiny Llama (config 1): 20 SPSA steps + one QK-Clip probe, fp32",
+           "ms_per_step": round(gpu_s * 1e3 / 20, 3), "probe_ms": round(gpu_probe_s * 1e3, 3),
+           "steps_applied": gpu_done}
+    ref_root = Path(os.environ.get("MUZO_REFERENCE_PATH", ROOT / "baseline" / "_ref"))
+    try:
+        if not (ref_root / "muzo_clip").is_dir():
+            raise ImportError(f"no reference package under {ref_root}")
+        sys.path.insert(0, str(ref_root))
+        from muzo_clip import MuZOClipOptimizer as RefOptimizer
+
+        threads = _cpu_baseline_module().use_all_threads()
+        cpu = torch.device("cpu")
+        ref_s, ref_probe_s, ref_done = _config1_run(RefOptimizer, cpu, lambda: None)
+        res["cpu_baseline"] = {"value": round(ref_s * 1e3 / 20, 3), "unit": "ms per step", "cores": threads,
+                               "kind": "reference", "probe_ms": round(ref_probe_s * 1e3, 3),
+                               "steps_applied": ref_done,
+                               "sample": "the reference package itself on CPU tensors (fp32), the same 20 steps "
+                                         "and probe"}
+    except ImportError as e:
+        res["cpu_baseline"] = {"unavailable": str(e)}
+    return res
+
+
 def run_case(args) -> int:
     if not args.sweep:
         return _run_one_case(args)
@@ -811,6 +878,8 @@ def _run_one_case(args) -> int:
                                    "kind": "port", "gbs": round(4.0 * numel / cpu_s / 1e9, 2),
                                    "sample": f"the reference's perturbation op sequence on CPU tensors ({args.dist} "
                                              f"noise from the CPU generator), median of 3 passes"}
+    elif args.case == "config1":
+        out.update(_run_config1(device))
     elif args.case == "attn":
         # one attention layer with the per-head max-logit side output (the fused capture path)
         # against SDPA plus the separate max-logit kernel on the same states
@@ -862,7 +931,8 @@ def _run_one_case(args) -> int:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", default=None, choices=["ns", "perturb", "rebuild", "apply", "normalize", "qk", "attn"],
+    ap.add_argument("--case", default=None,
+                    choices=["ns", "perturb", "rebuild", "apply", "normalize", "qk", "attn", "config1"],
                     help="run one kernel family on a small workload instead of the optimizer step")
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)
