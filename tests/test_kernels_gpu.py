@@ -288,11 +288,13 @@ def _gemm_case(device, m, n, k, batch, a_mn, b_mn, epi):
     assert bad == 0, f"{bad} mismatches, max err {err.max().item()}"
 
 
-@pytest.fixture(params=["pair", "single"])
+@pytest.fixture(params=["wide", "pair", "single"])
 def gemm_kernel(request, monkeypatch):
-    """Outputs of at least 256 x 256 run on the CTA-pair kernel (256 x 256 tiles over two SMs)
-    unless MUZO_GEMM_PAIR=0 selects the one-SM kernel (128 x 256 tiles): both are checked."""
-    monkeypatch.setenv("MUZO_GEMM_PAIR", "1" if request.param == "pair" else "0")
+    """Outputs of at least 256 rows and 512 columns run on the wide CTA-pair kernel (256 x 512
+    tiles over two SMs), MUZO_GEMM_WIDE=0 selects the 256 x 256 pair kernel there, and
+    MUZO_GEMM_PAIR=0 the one-SM kernel (128 x 256 tiles): all three are checked."""
+    monkeypatch.setenv("MUZO_GEMM_PAIR", "0" if request.param == "single" else "1")
+    monkeypatch.setenv("MUZO_GEMM_WIDE", "1" if request.param == "wide" else "0")
     return request.param
 
 

@@ -20,9 +20,13 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["pair", "single"])
+@pytest.fixture(params=["wide", "pair", "single"])
 def gemm_kernel(request, monkeypatch):
-    monkeypatch.setenv("MUZO_GEMM_PAIR", "1" if request.param == "pair" else "0")
+    """The 512 x 768 output runs on the wide pair kernel (256 x 512 tiles, its second tile column
+    half empty), on the 256 x 256 pair kernel with MUZO_GEMM_WIDE=0, on one SM with
+    MUZO_GEMM_PAIR=0."""
+    monkeypatch.setenv("MUZO_GEMM_PAIR", "0" if request.param == "single" else "1")
+    monkeypatch.setenv("MUZO_GEMM_WIDE", "1" if request.param == "wide" else "0")
     return request.param
 
 
