@@ -185,7 +185,7 @@ class ClockSampler:
 # gpu__time_duration.sum, dram__bytes_read.sum, dram__bytes_write.sum, --clock-control none, on
 # `python bench.py --steps 1 --warmup 1 --no-cpu-baseline --no-variant`): read + write of the
 # timed step, summed over its 105 ns_gemm launches, per perturbation pass and for the rebuild.
-NS_DRAM_BYTES_PER_STEP = 399.9e9
+NS_DRAM_BYTES_PER_STEP = 462.2e9
 PERTURB_DRAM_BYTES_PER_PASS = 27.89e9          # a pass that regenerates its noise
 PERTURB_KEPT_DRAM_BYTES_PER_PASS = 41.92e9     # mean of the keeping pass and the two kept passes
 REBUILD_KEPT_DRAM_BYTES_PER_STEP = 139.52e9
@@ -428,7 +428,7 @@ def run_gpu(args) -> int:
             "ns_tflops": round(ns_tflops, 1),
             "roofline": {
                 "bound": "tensor",
-                "kernel": "ns_gemm_pair_kernel / ns_gemm_kernel (Newton-Schulz GEMMs; all launches of the timed steps)",
+                "kernel": "ns_gemm_wide_kernel / ns_gemm_kernel (Newton-Schulz GEMMs; all launches of the timed steps)",
                 "achieved": round(ns_tflops, 1),
                 "peak": peaks["bf16_tflops_sustained"],
                 "unit": "TFLOP/s",
