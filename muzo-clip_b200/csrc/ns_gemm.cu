@@ -1114,15 +1114,16 @@ ns_gemm_wide_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       };
       // TMA load of E for the first live chunk at or after `from` (lane 0 issues)
       auto issue_e = [&](int from) {
-        if (EPI == MUZO_EPI_STORE) return;
-        for (int s2 = from; s2 < 8; ++s2) {
-          if (!live(s2)) continue;
-          if (lane == 0) {
-            mbar_arrive_expect_tx(ebar, W_EPI_BOX);
-            tma_load_3d(&map_e, ebar, ebox, c0_of(s2), r0, static_cast<int>(b));
+        if constexpr (EPI != MUZO_EPI_STORE) {
+          for (int s2 = from; s2 < 8; ++s2) {
+            if (!live(s2)) continue;
+            if (lane == 0) {
+              mbar_arrive_expect_tx(ebar, W_EPI_BOX);
+              tma_load_3d(&map_e, ebar, ebox, c0_of(s2), r0, static_cast<int>(b));
+            }
+            e_pending = true;
+            return;
           }
-          e_pending = true;
-          return;
         }
       };
       issue_e(0);
