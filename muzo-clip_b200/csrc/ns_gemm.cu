@@ -1172,6 +1172,13 @@ ns_gemm_wide_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
               const uint4 v = *reinterpret_cast<const uint4*>(ebox + sw64(lane, u));
               ew[4 * u] = v.x; ew[4 * u + 1] = v.y; ew[4 * u + 2] = v.z; ew[4 * u + 3] = v.w;
             }
+            // The next E box is written by the TMA unit (async proxy) over these plain shared
+            // loads, which a warp barrier alone does not wait for: a late load once returned the
+            // next chunk's values. A store that depends on every load issues only after all of
+            // them have landed (it writes into this lane's own row of the box, which the next
+            // load overwrites), and the proxy fence orders it before the async write.
+            *reinterpret_cast<volatile uint32_t*>(ebox + sw64(lane, 0)) = ew[3] ^ ew[7] ^ ew[11] ^ ew[15];
+            fence_proxy_async_smem();
             __syncwarp();
             issue_e(s2 + 1);
           }

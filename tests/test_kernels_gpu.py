@@ -311,6 +311,57 @@ def test_ns_gemm_shapes(device, gemm_kernel, m, n, k, batch):
         _gemm_case(device, m, n, k, batch, a_mn, b_mn, 2)
 
 
+def test_ns_gemm_wide_epilogue_is_deterministic(device):
+    """The wide kernel's fused epilogues at the step's size (a X + B X, 4096 x 14336 x 4096, and
+    b A + c A A on all and on upper-triangle tiles, batch 16): repeated launches are bit-identical
+    and the update matches the fp32 reference. E reaches the epilogue through a shared-memory box
+    that a TMA load refills while the previous chunk's values are read; before those reads were
+    ordered before the refill, a late read occasionally returned the next chunk's E."""
+    L = _lib()
+    g = torch.Generator(device="cpu").manual_seed(21)
+    m, n, batch, a = 4096, 14336, 16, 3.4445
+    X = (torch.randn((batch, m, n), generator=g) / (m * n) ** 0.5).to(torch.bfloat16).to(device)
+    Bm = (torch.randn((batch, m, m), generator=g) * 0.01).to(torch.bfloat16).to(device)
+    Bm = ((Bm.float() + Bm.float().mT) * 0.5).to(torch.bfloat16)
+    status = torch.zeros(4, dtype=torch.int32, device=device)
+    sp = L.stream_ptr(device)
+
+    def update():
+        Y = torch.zeros_like(X)
+        L.check(L.lib.muzo_ns_gemm(Bm.data_ptr(), m, m * m, 0, X.data_ptr(), n, m * n, 1, Y.data_ptr(), n, m * n,
+                                   X.data_ptr(), L.EPI_UPDATE, a, 0.0, m, n, m, batch, 0, None, None, None,
+                                   status.data_ptr(), sp), "update")
+        return Y
+
+    def poly(sym):
+        D = torch.zeros_like(Bm)
+        L.check(L.lib.muzo_ns_gemm(Bm.data_ptr(), m, m * m, 0, Bm.data_ptr(), m, m * m, 1, D.data_ptr(), m, m * m,
+                                   Bm.data_ptr(), L.EPI_POLY, -4.775, 2.0315, m, m, m, batch, sym, None, None, None,
+                                   status.data_ptr(), sp), "poly")
+        return D
+
+    first = update()
+    for _ in range(3):
+        assert torch.equal(update(), first)
+    for sym in (1, 0):
+        d0 = poly(sym)
+        for _ in range(3):
+            assert torch.equal(poly(sym), d0)
+    torch.cuda.synchronize()
+    assert status.tolist() == [0, 0, 0, 0]
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for j in range(0, batch, 4):   # fp32 reference in slices of 4 matrices
+            acc = torch.matmul(Bm[j:j + 4].float(), X[j:j + 4].float())
+            r = lambda t: t.to(torch.bfloat16).float()  # noqa: E731
+            ref = r(r(a * X[j:j + 4].float()) + r(acc))
+            tol = 2.0 ** -7 * (ref.abs() + r(acc).abs() + a * X[j:j + 4].float().abs()) + 1e-3
+            assert int(((first[j:j + 4].float() - ref).abs() > tol).sum()) == 0
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_tf32
+
+
 @pytest.mark.parametrize("m,k,batch,tall", [(512, 384, 2, False), (1024, 4096, 1, False), (300, 200, 2, True),
                                             (256, 688, 1, True), (776, 136, 1, False)])
 def test_ns_gemm_symmetric_outputs(device, gemm_kernel, m, k, batch, tall):
