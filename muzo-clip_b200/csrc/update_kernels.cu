@@ -76,22 +76,42 @@ ns_normalize_kernel(const muzo_segment* __restrict__ segs, int nsegs, const doub
   if (v.local_item0 == 0 && threadIdx.x == 0 && (!(m2 > 0.0) || !isfinite(m2)))
     atomicOr(flags + v.block, MUZO_FLAG_ZERO_NORM);
   const bool vec = aligned16(v.out);
+  // two vectors per trip, both loaded before either is stored: two 16-byte loads in flight per
+  // thread instead of one
 #pragma unroll 1
-  for (int it = 0; it < kItemsPerThread; ++it) {
-    const int64_t item = v.local_item0 + it * kElemThreads + threadIdx.x;
-    const int64_t li = item * 8;
-    if (li >= v.numel) break;
-    if (vec && li + 8 <= v.numel) {
-      float x[8];
-      load8(v.out, li, MUZO_BF16, x);
+  for (int it = 0; it < kItemsPerThread; it += 2) {
+    const int64_t li0 = (v.local_item0 + it * kElemThreads + threadIdx.x) * 8;
+    const int64_t li1 = li0 + static_cast<int64_t>(kElemThreads) * 8;
+    if (li0 >= v.numel) break;
+    if (vec && li1 + 8 <= v.numel) {
+      float x0[8], x1[8];
+      load8(v.out, li0, MUZO_BF16, x0);
+      load8(v.out, li1, MUZO_BF16, x1);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = bf16_quotient(x[k], denom, recip);
-      store8(v.out, li, MUZO_BF16, x);
-    } else {
+      for (int k = 0; k < 8; ++k) {
+        x0[k] = bf16_quotient(x0[k], denom, recip);
+        x1[k] = bf16_quotient(x1[k], denom, recip);
+      }
+      store8(v.out, li0, MUZO_BF16, x0);
+      store8(v.out, li1, MUZO_BF16, x1);
+      continue;
+    }
+#pragma unroll 1
+    for (int j = 0; j < 2; ++j) {
+      const int64_t li = j == 0 ? li0 : li1;
+      if (li >= v.numel) break;
+      if (vec && li + 8 <= v.numel) {
+        float x[8];
+        load8(v.out, li, MUZO_BF16, x);
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (li + k < v.numel)
-          store_elem(v.out, li + k, MUZO_BF16, __fdiv_rn(load_elem(v.out, li + k, MUZO_BF16), denom));
+        for (int k = 0; k < 8; ++k) x[k] = bf16_quotient(x[k], denom, recip);
+        store8(v.out, li, MUZO_BF16, x);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (li + k < v.numel)
+            store_elem(v.out, li + k, MUZO_BF16, __fdiv_rn(load_elem(v.out, li + k, MUZO_BF16), denom));
+      }
     }
   }
 }
