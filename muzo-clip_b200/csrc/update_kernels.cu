@@ -308,6 +308,21 @@ apply_update_kernel(const muzo_segment* __restrict__ segs, int nsegs, const floa
     const int64_t li = item * 8;
     if (li >= v.numel) break;
     float x[8], w[8];
+    const int64_t li1 = li + static_cast<int64_t>(kElemThreads) * 8;
+    if (vec && (it & 1) == 0 && it + 1 < kItemsPerThread && li1 + 8 <= v.numel) {
+      // two items per trip, all four vectors loaded before either result is stored
+      float x1[8], w1[8];
+      load8(v.out, li, MUZO_BF16, x);
+      load8(v.param, li, DTYPE, w);
+      load8(v.out, li1, MUZO_BF16, x1);
+      load8(v.param, li1, DTYPE, w1);
+      apply8<DTYPE>(x, w, sc, scale, neg_lr, apply_decay, decay);
+      apply8<DTYPE>(x1, w1, sc, scale, neg_lr, apply_decay, decay);
+      store8(v.param, li, DTYPE, w);
+      store8(v.param, li1, DTYPE, w1);
+      ++it;
+      continue;
+    }
     if (vec && li + 8 <= v.numel) {
       load8(v.out, li, MUZO_BF16, x);
       load8(v.param, li, DTYPE, w);
