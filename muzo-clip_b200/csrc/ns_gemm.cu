@@ -2,13 +2,15 @@
 // operands staged in shared memory by TMA tensor copies (each CTA fills only its own tiles), and the
 // element-wise parts of the quintic iteration (newton_schulz.py:55-58) fused into the epilogue.
 //
-// Two kernels share the tile enumeration and the epilogue: the CTA-pair kernel (256 x 256 tiles,
-// tcgen05.mma.cta_group::2 over two SMs; default when both output extents are >= 256) and the
-// one-SM kernel below (128 x 256 tiles; small outputs). The pair kernel stages 32 KB of operands
-// per SM and k-block where the one-SM kernel stages 48 KB for the same flops: measured 7-8 %
-// faster on the 4096 x 4096 / 4096 x 14336 / 14336 x 4096 Newton-Schulz batches. Its output
-// tiles are handed out in order by an atomic counter kept in the caller's status buffer, so
-// pairs delayed by other kernels on the GPU take fewer tiles.
+// Three kernels share the tile enumeration and the epilogue arithmetic: the wide CTA-pair kernel
+// (256 x 512 tiles as two 256 x 256 halves, tcgen05.mma.cta_group::2 over two SMs; default when
+// the output has >= 256 rows and >= 512 columns), the CTA-pair kernel (256 x 256 tiles; outputs
+// of 256 x 256 and more with fewer than 512 columns) and the one-SM kernel below (128 x 256
+// tiles; small outputs). Per flop, the pair kernel stages two thirds of the one-SM kernel's
+// operand bytes from L2 (32 instead of 48 KB per SM and k-block of 64) and the wide kernel half
+// (48 KB per SM for twice the flops), which is what keeps the tensor pipe fed. Output tiles of
+// the pair kernels are handed out in order by an atomic counter kept in the caller's status
+// buffer, so pairs delayed by other kernels on the GPU take fewer tiles.
 //
 // One-SM kernel: one persistent CTA per SM (grid = min(tiles, SMs)), 6 warps:
 //   warp 0      TMA producer (one thread): A/B k-blocks into a 4-stage shared-memory ring;
